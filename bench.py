@@ -1,0 +1,318 @@
+#!/usr/bin/env python
+"""Benchmark of the fused QK-RMSNorm + RoPE + non-causal attention op.
+
+Workload (the metric's config): Flux.1 joint
+attention at 1024x1024, B1 H24 S4608 D128, bf16, QK-RMSNorm + 3-axis RoPE.
+A step is one fused call over one batch element's (b, h) units. With N GPUs
+each rank runs its own batch element (batch x head partition, no
+collective): weak scaling, global batch N.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+`--impl reference` times the reference's algorithm on the host cores: the
+C++ restatement of the shader sequence (oracle/, the reference itself cannot
+be built or run here), on a bounded row sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "llm-runner_b200"))
+
+METRIC = "Flux joint-attn TFLOP/s per GPU (B1 H24 D128 S4608 bf16); % of BF16 peak"
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default="flux_1024")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["bf16_tflops"]), float(d.get("hbm_gbs", 0.0)), "measured"
+    return FALLBACK_PEAK_TFLOPS, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-i", str(device_index), "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons, power = [], [], set(), []
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, val in zip(self.NAMES, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        # "under load": samples drawing more than 40% of the highest power seen
+        pmax = max(power)
+        loaded = [s for s, p in zip(sm, power) if p >= 0.4 * pmax] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": max(mx),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(case, prep, budget_s=12.0, rows_per_chunk=512):
+    """The oracle (reference algorithm restated) on host cores over a bounded
+    row sample of one batch element. Returns (TFLOP/s, rows, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    S, H, D = case.seq_len, case.n_heads, case.head_dim
+
+    def run(rows):
+        t0 = time.perf_counter()
+        O.attention_block(prep.q[0], prep.k[0], prep.v[0], H, D, case.scale, eps=case.eps,
+                          q_gain=prep.q_gain, k_gain=prep.k_gain,
+                          split_row=min(case.split_row, S), cos=prep.cos, sin=prep.sin,
+                          exact=case.exact, rows=(0, rows))
+        return time.perf_counter() - t0
+
+    # A short probe sizes one timed call to about `budget_s` seconds.
+    probe = min(S, 128)
+    dt = run(probe)
+    rows = int(min(S, max(probe, probe * budget_s / max(dt, 1e-3))) // 16 * 16) or 16
+    dt = run(rows)
+    flops = 4.0 * H * rows * S * D
+    return flops / dt / 1e12, rows, dt
+
+
+def config_block(case, n):
+    return {"workload": f"{case.name}: B{case.batch} H{case.n_heads} S{case.seq_len} "
+                        f"D{case.head_dim} {case.dtype}, QK-RMSNorm + RoPE + non-causal attention",
+            "batch_per_gpu": case.batch, "global_batch": case.batch * n,
+            "n_heads": case.n_heads, "seq_len": case.seq_len, "head_dim": case.head_dim,
+            "parallelism": f"batch x head partition over {n} GPU(s), no collective",
+            "l2": "flushed (256 MiB write) between timed steps"}
+
+
+def run_reference(args):
+    """CPU reference arm: rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    case = C.CASES[args.config]
+    prep = C.prepare(case, L.rope_tables)
+    S, H, D = case.seq_len, case.n_heads, case.head_dim
+    rows = 128
+    times, r0 = [], 0
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        O.attention_block(prep.q[0], prep.k[0], prep.v[0], H, D, case.scale, eps=case.eps,
+                          q_gain=prep.q_gain, k_gain=prep.k_gain,
+                          split_row=min(case.split_row, S), cos=prep.cos, sin=prep.sin,
+                          exact=case.exact, rows=(r0, r0 + rows))
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+        r0 = (r0 + rows) % S
+    ms = 1e3 * sum(times) / len(times)
+    tflops = 4.0 * H * rows * S * D / (ms / 1e3) / 1e12
+    cores = os.cpu_count()
+    sample = (f"per step: {rows} query rows x {H} heads of one batch element, full "
+              f"S={S} keys (norm+transpose+RoPE over all tokens, then flash_attention_v2)")
+    line = {"metric": METRIC, "value": tflops, "unit": "TFLOP/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32 (fp16 operands)", "data": "synthetic",
+            "config": config_block(case, args.gpus),
+            "cpu_baseline": {"value": tflops, "unit": "TFLOP/s", "cores": cores,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": tflops, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0},
+            "note": "reference (C3 + Slang + Vulkan) cannot be built or run here; this is "
+                    "the oracle's line-by-line C++ restatement of its shaders"}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import to_device
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    case = C.CASES[args.config]
+    prep = C.prepare(case, L.rope_tables)
+    # Each rank owns one batch element; make its inputs distinct.
+    if rank:
+        rng = np.random.default_rng(case.seed * 1000 + rank)
+        for a in (prep.q, prep.k, prep.v):
+            a[...] = C.round_to(rng.standard_normal(a.shape, dtype=np.float32), case.dtype)
+    dc = to_device(prep, device=local)
+    ctx = L.Context(local)
+    ctx.reserve(L.workspace_bytes(dc.desc()))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+    flops = case.flops  # per rank (one batch element)
+
+    sampler = ClockSampler(local)
+    ctx.profile(True)
+    t_warm = time.perf_counter()
+    i = 0
+    while i < max(args.warmup, 3) or time.perf_counter() - t_warm < 1.5:
+        flush.zero_()
+        dc.run(ctx)
+        torch.cuda.synchronize()
+        i += 1
+    ctx.sync()
+
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    attn_ms, pro_ms = [], []
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    l0 = ctx.launches
+    for k in range(args.steps):
+        flush.zero_()
+        ev[k][0].record()
+        dc.run(ctx)
+        ev[k][1].record()
+        p, a = ctx.profile_read()  # waits for this step
+        pro_ms.append(p)
+        attn_ms.append(a)
+    torch.cuda.synchronize()
+    launches = ctx.launches - l0
+    if world > 1:
+        dist.barrier()
+    ctx.sync()
+    total_ms = sum(s.elapsed_time(e) for s, e in ev)
+    t = torch.tensor([total_ms], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms = float(t.item())
+    ms_step = total_ms / args.steps
+    value = world * flops / (ms_step / 1e3) / 1e12
+
+    # End to end through the public API: pinned host inputs -> device, the
+    # fused op, result -> pinned host, every step.
+    hq, hk, hv = (x.cpu().pin_memory() for x in (dc.q, dc.k, dc.v))
+    ho = torch.empty(dc.o.shape, dtype=dc.o.dtype).pin_memory()
+    e2e_steps = min(args.steps, 20)
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(e2e_steps)]
+    ctx.profile(False)
+    torch.cuda.synchronize()
+    for k in range(e2e_steps):
+        flush.zero_()
+        e2e_ev[k][0].record()
+        dc.q.copy_(hq, non_blocking=True)
+        dc.k.copy_(hk, non_blocking=True)
+        dc.v.copy_(hv, non_blocking=True)
+        dc.run(ctx)
+        ho.copy_(dc.o, non_blocking=True)
+        e2e_ev[k][1].record()
+    torch.cuda.synchronize()
+    ctx.sync()
+    e2e_ms = sum(s.elapsed_time(e) for s, e in e2e_ev) / e2e_steps
+    te = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    clocks = sampler.stop()
+
+    peak, hbm, peak_kind = peaks()
+    a_ms = statistics.mean(attn_ms)
+    achieved = flops / (a_ms / 1e3) / 1e12
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "fa_fwd_tc_flux_traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get("dram_bytes_per_launch")
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) bf16 Q/K/V, U(0.8,1.2) gains)",
+        "config": config_block(case, world),
+        "value_per_gpu": value / world,
+        "pct_of_peak": 100.0 * (value / world) / peak,
+        "phases_ms": {"prologue": statistics.mean(pro_ms), "attention": a_ms},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
+                     "kernel": "fa_fwd_tc_kernel<128, bf16>",
+                     "peak_source": f"{peak_kind} bf16_tflops (burst)"},
+        "e2e": {"value": world * flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+                "h2d_bytes_per_step": 3 * dc.q.numel() * dc.q.element_size(),
+                "d2h_bytes_per_step": dc.o.numel() * dc.o.element_size(),
+                "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tf, rows, dt = cpu_sample(case, prep)
+        line["cpu_baseline"] = {
+            "value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{rows} of {case.seq_len} query rows x {case.n_heads} heads, "
+                      f"{dt:.1f} s, oracle restatement of the reference shaders"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,223 @@
+/*
+ * llmr_attn — B200 (sm_100a) drop-in for llm-runner's fused non-causal
+ * attention path: per-head QK-RMSNorm, multi-axis RoPE and flash attention.
+ *
+ * This C ABI replaces, for this op only, the Vulkan dispatch and buffer layer
+ * that the reference's model code records attention through
+ * (lib/vulkan/graph.c3:47-72 RenderGraph.dispatch -> lib/vulkan/compute.c3:86
+ * dispatch_kernel, buffers from lib/model/tensor.c3:8-120). Paths cited below
+ * are relative to the reference project root.
+ *
+ * Conventions
+ *  - Every call returns an int status (LLMR_OK = 0). llmr_last_error() gives a
+ *    one-line message for the last failure on that context.
+ *  - Device buffers are caller-owned (as llm::Tensor is). The mirrors of the
+ *    reference ops take fp32 device buffers in the reference's layouts.
+ *  - Calls are asynchronous on the context's CUDA stream; llmr_sync() is the
+ *    equivalent of RenderGraph.checkpoint()/flush() (lib/vulkan/graph.c3:96-107)
+ *    and is where device-side timeouts surface as LLMR_ETIMEOUT.
+ *  - A context is bound to one device and is not thread-safe, as the
+ *    reference's single command buffer per context is not
+ *    (lib/vulkan/context.c3:328-334). Use one context per host thread / GPU.
+ *  - The hot calls never allocate: scratch comes from the workspace sized at
+ *    llmr_ctx_create() (or grown explicitly with llmr_ctx_reserve()).
+ */
+#ifndef LLMR_ATTN_H
+#define LLMR_ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. Replace the reference's faultdef set
+ * (lib/vulkan/context.c3:10: NO_SUITABLE_DEVICE, COMPUTE_ERROR, ...). */
+enum {
+  LLMR_OK = 0,
+  LLMR_EINVAL = 1,      /* bad argument / unsupported shape */
+  LLMR_ENOMEM = 2,      /* allocation failed or workspace too small */
+  LLMR_ECUDA = 3,       /* CUDA runtime / driver error */
+  LLMR_ENCCL = 4,       /* NCCL error (ring variant) */
+  LLMR_ETIMEOUT = 5,    /* a bounded device-side wait gave up */
+  LLMR_ENODEV = 6       /* no usable sm_100 device */
+};
+
+typedef enum { LLMR_F32 = 0, LLMR_F16 = 1, LLMR_BF16 = 2 } llmr_dtype;
+
+/* Q/K/V/O tensor layouts.
+ * BSHD: [batch][seq][head][dim] — the reference's activation layout
+ *       [S, H*D] per batch element (dependencies/zimage.c3l/dit.c3:1445-1449).
+ * BHSD: [batch][head][seq][dim] — the reference's post-transpose_heads layout
+ *       (dependencies/zimage.c3l/shaders/zimage.slang:563-601). */
+typedef enum { LLMR_LAYOUT_BSHD = 0, LLMR_LAYOUT_BHSD = 1 } llmr_layout;
+
+/* Flags for llmr_attn_desc.flags. */
+enum {
+  LLMR_NORM_Q = 1u << 0,  /* per-head RMSNorm on Q (batch_head_norm) */
+  LLMR_NORM_K = 1u << 1,  /* per-head RMSNorm on K */
+  LLMR_ROPE = 1u << 2,    /* multi-axis RoPE on Q and K (mrope) from tables */
+  LLMR_EXACT = 1u << 3,   /* fp32 operands and exact softmax (spatial_attention
+                             math, lib/shaders/diffusion.slang:478-569) instead
+                             of fp16 operands (flash_attention_v2 math) */
+  LLMR_LSE = 1u << 4      /* also write log-sum-exp (natural log) per row */
+};
+
+typedef struct llmr_ctx llmr_ctx;
+
+/* Create a context on CUDA device `device`, using `stream` (a cudaStream_t;
+ * NULL = a new non-blocking stream owned by the context) and a device
+ * workspace of `workspace_bytes` (may be 0 and grown by llmr_ctx_reserve).
+ * Replaces createContext() (lib/vulkan/context.c3:73). */
+int llmr_ctx_create(int device, size_t workspace_bytes, void *stream,
+                    llmr_ctx **out);
+int llmr_ctx_destroy(llmr_ctx *ctx);
+/* Grow the workspace to at least `bytes` (synchronous; not for the hot loop). */
+int llmr_ctx_reserve(llmr_ctx *ctx, size_t bytes);
+int llmr_set_stream(llmr_ctx *ctx, void *stream);
+void *llmr_get_stream(llmr_ctx *ctx);
+const char *llmr_last_error(llmr_ctx *ctx);
+/* Wait for all work on the context stream; reports device-side timeouts.
+ * Replaces RenderGraph.checkpoint/flush (lib/vulkan/graph.c3:96-107). */
+int llmr_sync(llmr_ctx *ctx);
+/* Number of kernels this context has launched (for launch accounting). */
+uint64_t llmr_launch_count(llmr_ctx *ctx);
+
+/* Per-phase GPU timing of llmr_attention_fused, the device-side counterpart
+ * of the reference's @prof_checkpoint phase timer (dependencies/zimage.c3l/
+ * dit.c3:17-26, "C:attn_all" at :1484). When enabled, each fused call
+ * records CUDA events around its prologue and attention kernels.
+ * llmr_profile_read waits for the last profiled call and writes
+ * ms[0] = prologue (0 if none ran), ms[1] = attention kernel. */
+int llmr_profile_enable(llmr_ctx *ctx, int on);
+int llmr_profile_read(llmr_ctx *ctx, float *ms2);
+
+/* Buffers. Replace create_tensor / upload_to_tensor / download_tensor
+ * (lib/model/tensor.c3:27-46, :79, :99). upload/download are synchronous,
+ * as the reference's staging copies are. */
+int llmr_alloc(llmr_ctx *ctx, size_t bytes, void **out);
+int llmr_free(llmr_ctx *ctx, void *ptr);
+int llmr_upload(llmr_ctx *ctx, void *dst_device, const void *src_host,
+                size_t bytes);
+int llmr_download(llmr_ctx *ctx, void *dst_host, const void *src_device,
+                  size_t bytes);
+
+/* ---- Mirrors of the reference's attention ops (fp32 buffers) ---------- */
+
+/* flash_attention_v2 (dependencies/zimage.c3l/shaders/flash_attn.slang:38-241;
+ * push constants FlashAttentionPC {head_dim, n_heads, seq_len, scale},
+ * dependencies/zimage.c3l/dit.c3:136-142). q,k,v: [n_heads, seq_len,
+ * head_dim]; o: [seq_len, n_heads*head_dim]. Operands are rounded to fp16 as
+ * the shader does. head_dim 64 or 128 (the shader itself is 128-only). */
+int llmr_flash_attention_v2(llmr_ctx *ctx, const float *q, const float *k,
+                            const float *v, float *o, uint32_t head_dim,
+                            uint32_t n_heads, uint32_t seq_len, float scale);
+
+/* batch_head_norm (dependencies/zimage.c3l/shaders/zimage.slang:623-659;
+ * BatchHeadNormPC {n_heads, head_dim, seq_len, eps}, dit.c3:128-134).
+ * In place on data[seq_len, n_heads*head_dim] with gain[head_dim]. */
+int llmr_batch_head_norm(llmr_ctx *ctx, float *data, const float *gain,
+                         uint32_t n_heads, uint32_t head_dim, uint32_t seq_len,
+                         float eps);
+
+/* perhead_rmsnorm (dependencies/qwen_edit.c3l/shaders/vit.slang:590-616;
+ * PerHeadRMSNormPC {seq_len, n_heads, head_dim, eps}). Same math. */
+int llmr_perhead_rmsnorm(llmr_ctx *ctx, float *data, const float *weight,
+                         uint32_t seq_len, uint32_t n_heads, uint32_t head_dim,
+                         float eps);
+
+/* transpose_heads (dependencies/zimage.c3l/shaders/zimage.slang:575-601;
+ * TransposeHeadsPC {seq_len, n_heads, head_dim, direction}, dit.c3:120-126).
+ * direction 0: [S,H,D] -> [H,S,D]; 1: reverse. in and out must not alias. */
+int llmr_transpose_heads(llmr_ctx *ctx, const float *in, float *out,
+                         uint32_t seq_len, uint32_t n_heads, uint32_t head_dim,
+                         uint32_t direction);
+
+/* mrope (dependencies/zimage.c3l/shaders/mrope.slang:33-54; MRoPEPC
+ * {seq_len, n_heads, pad, pad}, dit.c3:164-170). In place on
+ * data[n_heads, seq_len, 128] with cos/sin[seq_len, 64]. */
+int llmr_mrope(llmr_ctx *ctx, float *data, const float *cos_t,
+               const float *sin_t, uint32_t seq_len, uint32_t n_heads);
+
+/* spatial_attention (lib/shaders/diffusion.slang:478-569;
+ * SpatialAttentionPC {head_dim, n_heads, seq_len, scale},
+ * dependencies/depth_anything.c3l/depth_anything.c3:335-337). q,k,v,o:
+ * [n_heads, seq_len, head_dim] fp32, exact softmax. `scores` is accepted for
+ * signature compatibility and ignored (may be NULL): no S x S buffer is
+ * materialised. head_dim 64 or 128. */
+int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k,
+                           const float *v, float *scores, float *o,
+                           uint32_t head_dim, uint32_t n_heads,
+                           uint32_t seq_len, float scale);
+
+/* split_qkv (dependencies/depth_anything.c3l/shaders/depth.slang:40-58;
+ * {dim, n_rows}): qkv[n_rows, 3*dim] -> q,k,v [n_rows, dim]. */
+int llmr_split_qkv(llmr_ctx *ctx, const float *qkv, float *q, float *k,
+                   float *v, uint32_t dim, uint32_t n_rows);
+
+/* ---- Fused op ---------------------------------------------------------- */
+
+/* One call for the reference's whole 8-dispatch attention sequence
+ * (batch_head_norm x2, transpose_heads x3, mrope x2, flash_attention_v2:
+ * dependencies/flux.c3l/flux_dit.c3:812-872, :1020-1047,
+ * dependencies/zimage.c3l/dit.c3:1445-1483, dependencies/qwen_edit.c3l/
+ * mmdit.c3:577-678, dependencies/depth_anything.c3l/depth_anything.c3:
+ * 610-630). Strides are in elements; 0 selects the dense default for the
+ * layout. A fused QKV buffer [S, 3*H*D] is addressed by passing q, k, v
+ * pointers at column offsets 0, H*D, 2*H*D with row stride 3*H*D (replaces
+ * split_qkv). O is always [B][S][H*D] (row stride o_row_stride). */
+typedef struct {
+  uint32_t batch, n_heads, seq_len, head_dim; /* head_dim 64 or 128 */
+  llmr_dtype in_dtype;                        /* dtype of q, k, v */
+  llmr_dtype out_dtype;                       /* dtype of o */
+  llmr_layout layout;                         /* layout of q, k, v */
+  uint32_t flags;                             /* LLMR_NORM_Q | ... */
+  float scale;                                /* softmax scale */
+  float eps;                                  /* RMSNorm epsilon */
+  /* Rows [0, split_row) use gain set 0, rows [split_row, S) gain set 1
+   * (txt/img gains, flux_dit.c3:812-845). q_gain/k_gain point to 2*head_dim
+   * fp32 device values when split_row > 0, else head_dim values. */
+  uint32_t split_row;
+  /* Row of the cos/sin tables that token 0 uses (sequence shards). */
+  uint32_t rope_row_offset;
+  /* Element strides; 0 = dense default. */
+  uint64_t q_row_stride, k_row_stride, v_row_stride, o_row_stride;
+  uint64_t q_batch_stride, k_batch_stride, v_batch_stride, o_batch_stride;
+  uint64_t q_head_stride, k_head_stride, v_head_stride;
+} llmr_attn_desc;
+
+/* Workspace bytes llmr_attention_fused needs for `desc`. */
+size_t llmr_attention_workspace_bytes(const llmr_attn_desc *desc);
+
+/* Fused QK-RMSNorm + RoPE + attention. cos_t/sin_t: fp32 device tables
+ * [rows, head_dim/2] (required with LLMR_ROPE). lse: fp32 [B][H][S] device
+ * buffer, written when LLMR_LSE is set (else may be NULL). */
+int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *desc,
+                         const void *q, const void *k, const void *v,
+                         const float *q_gain, const float *k_gain,
+                         const float *cos_t, const float *sin_t, void *o,
+                         float *lse);
+
+/* Merge two normalised partial attention results over disjoint key sets
+ * (o_a, lse_a) and (o_b, lse_b) into (o_a, lse_a): the combine step of the
+ * sequence-sharded ring. o_*: fp32 [rows][n_heads*head_dim] (row stride
+ * o_row_stride elements), lse_*: fp32 [n_heads][rows]. No reference
+ * counterpart: the reference is single-GPU. */
+int llmr_attention_merge(llmr_ctx *ctx, float *o_a, float *lse_a,
+                         const float *o_b, const float *lse_b, uint32_t rows,
+                         uint32_t n_heads, uint32_t head_dim,
+                         uint64_t o_row_stride);
+
+/* Host-side multi-axis RoPE table builder (precompute_flux_mrope,
+ * dependencies/flux.c3l/flux_dit.c3:396-525; precompute_mrope_tables,
+ * dependencies/zimage.c3l/dit.c3:561-757): pos is [seq_len][n_axes] int32,
+ * outputs cos/sin [seq_len][sum(axes_dims)/2] fp32 in HOST memory. */
+int llmr_rope_tables(const int32_t *pos, uint32_t seq_len, uint32_t n_axes,
+                     const uint32_t *axes_dims, float theta, float *cos_out,
+                     float *sin_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLMR_ATTN_H */

@@ -1,0 +1,399 @@
+// Non-causal flash attention forward for sm_100a on the 5th-generation
+// tensor cores (tcgen05), fp16 operands, fp32 accumulation in TMEM.
+//
+// Computes, per (batch, head), O = softmax(scale * Q K^T) V with the same
+// operand rounding as the reference shader (Q, K, V and P held as fp16,
+// scores / softmax state / O accumulated in fp32:
+// dependencies/zimage.c3l/shaders/flash_attn.slang:61-64, :98-101, :197-201,
+// :113-118). Rows and keys beyond seq_len are masked exactly as :120-121 do.
+//
+// CTA = 2 query tiles of 128 rows of one (b, h) = 256 queries; 320 threads:
+//   warps 0-3  softmax warpgroup for tile 0 (thread i owns query row i)
+//   warps 4-7  softmax warpgroup for tile 1
+//   warp  8    TMA producer: Q once, then K_j, V_j into an NST-slot ring
+//   warp  9    MMA issuer (one elected lane) + TMEM owner
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D)
+// P_t (fp16x2) overwrites the first 64 columns of S_t after it is read.
+// MMA order per key block j (ping-pong, so one tile's softmax overlaps the
+// other tile's GEMMs):
+//   PV0_j, S0_{j+1}, PV1_j, S1_{j+1}
+// The softmax rescales O lazily: only when a row max grows by more than
+// 2^8 over the max used so far (so fp16 P stays <= 256).
+#pragma once
+#include "ptx.cuh"
+
+namespace llmr {
+
+struct FaParams {
+  int S;                 // sequence length (queries = keys)
+  int H;                 // heads; blockIdx.y = b * H + h
+  float scale_log2;      // softmax scale * log2(e)
+  void *o;               // output base (OutT)
+  long long o_row_stride;    // elements between consecutive tokens
+  long long o_batch_stride;  // elements between batch elements
+  float *lse;            // optional [B][H][S] natural-log LSE
+  int *err;              // device error word (nonzero on timeout)
+};
+
+template <int D>
+struct FaCfg {
+  static constexpr int BM = 128;                 // query rows per tile
+  static constexpr int BN = 128;                 // keys per block
+  static constexpr int CHUNK_BYTES = 128 * 128;  // one 64-col x 128-row SW128 box
+  static constexpr int NCHUNK = D / 64;
+  static constexpr int TILE_BYTES = BM * D * 2;  // one Q/K/V tile, fp16
+  static constexpr int NST = D == 128 ? 4 : 8;   // K/V ring slots
+  static constexpr int Q_OFF = 0;
+  static constexpr int KV_OFF = 2 * TILE_BYTES;
+  static constexpr int BAR_OFF = KV_OFF + NST * TILE_BYTES;
+  // barriers: q_full, kv_full[NST], kv_empty[NST], s_full[2], p_full[2],
+  // o_full, drain ; then tmem base word and abort flag
+  static constexpr int NBAR = 1 + 2 * NST + 2 + 2 + 1 + 1;
+  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;  // +align slack
+  static constexpr int THREADS = 320;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t O_COL = 256;
+};
+
+// Keeps every use of registers filled by tcgen05.ld after tcgen05.wait::ld.
+__device__ __forceinline__ void reg_fence32(uint32_t *r) {
+#pragma unroll
+  for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
+}
+
+template <typename OutT>
+__device__ __forceinline__ void store_row_chunk(OutT *dst, const float *v);
+
+template <>
+__device__ __forceinline__ void store_row_chunk<float>(float *dst,
+                                                       const float *v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4)
+    *reinterpret_cast<float4 *>(dst + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+}
+template <>
+__device__ __forceinline__ void store_row_chunk<__half>(__half *dst,
+                                                        const float *v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 u;
+    u.x = pack_f16x2(v[i], v[i + 1]);
+    u.y = pack_f16x2(v[i + 2], v[i + 3]);
+    u.z = pack_f16x2(v[i + 4], v[i + 5]);
+    u.w = pack_f16x2(v[i + 6], v[i + 7]);
+    *reinterpret_cast<uint4 *>(dst + i) = u;
+  }
+}
+template <>
+__device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(
+    __nv_bfloat16 *dst, const float *v) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 8) {
+    uint4 u;
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[i], v[i + 1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+    __nv_bfloat162 c = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+    __nv_bfloat162 d = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+    u.x = *reinterpret_cast<uint32_t *>(&a);
+    u.y = *reinterpret_cast<uint32_t *>(&b);
+    u.z = *reinterpret_cast<uint32_t *>(&c);
+    u.w = *reinterpret_cast<uint32_t *>(&d);
+    *reinterpret_cast<uint4 *>(dst + i) = u;
+  }
+}
+
+template <int D, typename OutT>
+__global__ void __launch_bounds__(320, 1)
+    fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV,
+                     const FaParams p) {
+  using C = FaCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment: SW128 atoms must start on 1024-byte boundaries so
+  // that the descriptors' base offset is 0.
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  uint8_t *sQ = smem + C::Q_OFF;
+  uint8_t *sKV = smem + C::KV_OFF;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+  uint64_t *q_full = bars;
+  uint64_t *kv_full = bars + 1;
+  uint64_t *kv_empty = bars + 1 + C::NST;
+  uint64_t *s_full = bars + 1 + 2 * C::NST;
+  uint64_t *p_full = s_full + 2;
+  uint64_t *o_full = p_full + 2;
+  uint64_t *drain = o_full + 1;
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int S = p.S;
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int q0 = blockIdx.x * 2 * C::BM;
+  const int nblk = (S + C::BN - 1) / C::BN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < C::NST; i++) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int t = 0; t < 2; t++) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+    }
+    mbar_init(o_full, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_base_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+      for (int t = 0; t < 2; t++)
+        for (int c = 0; c < C::NCHUNK; c++)
+          tma_load_4d(sQ + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, q_full,
+                      c * 64, q0 + t * C::BM, h, b);
+      bool ok = true;
+      int issued = 0;  // K/V tile loads armed so far
+      for (int j = 0; j < nblk && ok; j++) {
+        for (int kind = 0; kind < 2; kind++) {
+          const int u = 2 * j + kind;
+          const int slot = u % C::NST, round = u / C::NST;
+          if (round > 0 && !mbar_wait(&kv_empty[slot], (round - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&kv_full[slot], C::TILE_BYTES);
+          const CUtensorMap *m = kind ? &tmV : &tmK;
+          for (int c = 0; c < C::NCHUNK; c++)
+            tma_load_4d(sKV + slot * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
+                        &kv_full[slot], c * 64, j * C::BN, h, b);
+          issued = u + 1;
+        }
+      }
+      if (!ok) {
+        // Abort path: let every armed copy land before the CTA exits.
+        mbar_wait_raw(q_full, 0, 100000000ull);
+        for (int u = issued - C::NST < 0 ? 0 : issued - C::NST; u < issued; u++)
+          mbar_wait_raw(&kv_full[u % C::NST], (u / C::NST) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t IDESC_S = idesc_f16_f32(128, C::BN, 0);
+      constexpr uint32_t IDESC_O = idesc_f16_f32(128, D, 1);
+      const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
+      auto issue_s = [&](int t, int slot) {
+        const uint32_t qa = sQa + t * C::TILE_BYTES;
+        const uint32_t ka = sKVa + slot * C::TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < D / 16; k++) {
+          const uint32_t off = (k >> 2) * C::CHUNK_BYTES + (k & 3) * 32;
+          mma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024),
+                 sdesc_sw128(ka + off, 16, 1024), IDESC_S, k > 0);
+        }
+      };
+      auto issue_o = [&](int t, int slot, bool acc) {
+        const uint32_t va = sKVa + slot * C::TILE_BYTES;
+#pragma unroll
+        for (int k = 0; k < C::BN / 16; k++) {
+          mma_ts(tmem + C::O_COL + t * D, tmem + t * 128 + k * 8,
+                 sdesc_sw128(va + k * 2048, C::CHUNK_BYTES, 1024), IDESC_O,
+                 (acc || k > 0) ? 1u : 0u);
+        }
+      };
+      bool ok = mbar_wait(q_full, 0, abort_flag);
+      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0, 0);
+        mma_commit(&s_full[0]);
+        issue_s(1, 0);
+        mma_commit(&s_full[1]);
+        mma_commit(&kv_empty[0]);
+      }
+      for (int j = 0; j < nblk && ok; j++) {
+        const int uV = 2 * j + 1, sV = uV % C::NST;
+        const int uK = 2 * j + 2, sK = uK % C::NST;
+        const bool more = j + 1 < nblk;
+        if (!mbar_wait(&kv_full[sV], (uV / C::NST) & 1, abort_flag)) break;
+        if (!mbar_wait(&p_full[0], j & 1, abort_flag)) break;
+        tc_fence_after();
+        issue_o(0, sV, j > 0);
+        if (more) {
+          if (!mbar_wait(&kv_full[sK], (uK / C::NST) & 1, abort_flag)) break;
+          tc_fence_after();
+          issue_s(0, sK);
+          mma_commit(&s_full[0]);
+        }
+        if (!mbar_wait(&p_full[1], j & 1, abort_flag)) break;
+        tc_fence_after();
+        issue_o(1, sV, j > 0);
+        mma_commit(&kv_empty[sV]);
+        if (more) {
+          issue_s(1, sK);
+          mma_commit(&s_full[1]);
+          mma_commit(&kv_empty[sK]);
+        }
+      }
+      mma_commit(o_full);
+      // Drain: every MMA this thread issued has completed before TMEM is
+      // released at the end of the kernel.
+      mma_commit(drain);
+      mbar_wait_raw(drain, 0, 100000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int t = warp >> 2;                  // query tile 0 or 1
+    const int row = threadIdx.x & 127;        // row within the tile = TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + lane_off + t * 128;
+    const uint32_t tO = tmem + lane_off + C::O_COL + t * D;
+    const float sl2 = p.scale_log2;
+    float m_used = -INFINITY;  // log2-domain max the P values are relative to
+    float l = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < nblk; j++) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const int valid = S - j * C::BN;  // keys of this block below seq_len
+      // Loads 32 score columns of this row, masking keys >= seq_len.
+      auto load_chunk = [&](int c, float *v) {
+        tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t *>(v));
+        tmem_wait_ld();
+        reg_fence32(reinterpret_cast<uint32_t *>(v));
+        if (valid < C::BN) {
+#pragma unroll
+          for (int i = 0; i < 32; i++)
+            if (c * 32 + i >= valid) v[i] = -INFINITY;
+        }
+      };
+      // P = 2^(s*scale*log2e - m_used) as fp16 into the chunk's 16 columns.
+      auto emit_chunk = [&](int c, const float *v, float neg_m) {
+        uint32_t pk[16];
+        float sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const float p0 = ex2_approx(fmaf(v[2 * i], sl2, neg_m));
+          const float p1 = ex2_approx(fmaf(v[2 * i + 1], sl2, neg_m));
+          sum += p0 + p1;
+          pk[i] = pack_f16x2(p0, p1);
+        }
+        tmem_st16(tS + c * 16, pk);
+        return sum;
+      };
+      float l_blk = 0.0f;
+      // Fast path: the max used so far stays within 2^8 of every score of
+      // this block, so each chunk is exponentiated as soon as it is loaded.
+      bool restart = (j == 0);
+      if (!restart) {
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          float v[32];
+          load_chunk(c, v);
+          float mc = v[0];
+#pragma unroll
+          for (int i = 1; i < 32; i++) mc = fmaxf(mc, v[i]);
+          if (__any_sync(0xffffffffu, mc * sl2 > m_used + 8.0f)) {
+            restart = true;
+            break;
+          }
+          l_blk += emit_chunk(c, v, -m_used);
+        }
+      }
+      if (restart) {
+        // Slow path: full row max first, then rescale O and l, then P.
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          float v[32];
+          load_chunk(c, v);
+#pragma unroll
+          for (int i = 0; i < 32; i++) mx = fmaxf(mx, v[i]);
+        }
+        const float m_new = mx * sl2;
+        const bool need = m_new > m_used + 8.0f;
+        const float m_tgt = need ? m_new : m_used;
+        const float factor = ex2_approx(m_used - m_tgt);  // 0 on the first block
+        l *= factor;
+        if (j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < D / 32; c++) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+#pragma unroll
+            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        m_used = m_tgt;
+        l_blk = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          float v[32];
+          load_chunk(c, v);
+          l_blk += emit_chunk(c, v, -m_used);
+        }
+      }
+      l += l_blk;
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[t]);
+    }
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, abort_flag));
+    if (ok) {
+      tc_fence_after();
+      const int qrow = q0 + t * C::BM + row;
+      const float inv_l = 1.0f / l;
+      OutT *dst = reinterpret_cast<OutT *>(p.o) + (long long)b * p.o_batch_stride +
+                  (long long)qrow * p.o_row_stride + (long long)h * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; c++) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[i]) * inv_l;
+        if (qrow < S) store_row_chunk<OutT>(dst + c * 32, v);
+      }
+      if (p.lse != nullptr && qrow < S)
+        p.lse[(long long)bh * S + qrow] = (m_used + log2f(l)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
+}
+
+}  // namespace llmr

@@ -1,0 +1,627 @@
+// C-ABI implementation of include/llmr_attn.h for sm_100a.
+//
+// Host side of the drop-in boundary: context and workspace management, TMA
+// tensor-map construction, argument validation and the kernel launches that
+// replace the reference's Vulkan dispatches for this op
+// (lib/vulkan/compute.c3:86-133 dispatch_kernel; the call sites are
+// dependencies/flux.c3l/flux_dit.c3:812-872, dependencies/zimage.c3l/
+// dit.c3:1445-1483, dependencies/qwen_edit.c3l/mmdit.c3:577-678,
+// dependencies/depth_anything.c3l/depth_anything.c3:610-630).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/llmr_attn.h"
+#include "fa_tc.cuh"
+#include "kernels_misc.cuh"
+
+using namespace llmr;
+
+struct llmr_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  void *ws = nullptr;
+  size_t ws_bytes = 0;
+  int *d_err = nullptr;
+  uint64_t launches = 0;
+  int num_sms = 0;
+  bool prof_on = false;
+  bool prof_valid = false;
+  cudaEvent_t prof_ev[3] = {nullptr, nullptr, nullptr};
+  std::string err;
+};
+
+namespace {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t,
+                                  void *, const cuuint64_t *, const cuuint64_t *,
+                                  const cuuint32_t *, const cuuint32_t *,
+                                  CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion,
+                                  CUtensorMapFloatOOBfill);
+
+int fail(llmr_ctx *ctx, int code, const char *fmt, ...) {
+  if (ctx) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    ctx->err = buf;
+  }
+  return code;
+}
+
+#define CUDA_TRY(ctx, call)                                                   \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess)                                                    \
+      return fail(ctx, LLMR_ECUDA, "%s: %s", #call, cudaGetErrorString(e_));  \
+  } while (0)
+
+// Checks the launch that was just enqueued.
+int after_launch(llmr_ctx *ctx, const char *what) {
+  ctx->launches++;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    return fail(ctx, LLMR_ECUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return LLMR_OK;
+}
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 4-D fp16 tensor map over (d, s, h, b) with a 64 x 128 x 1 x 1 box and
+// 128-byte swizzle: one box is one SW128 K-major operand chunk.
+int make_map(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S,
+             int H, int B, long long rs, long long hs, long long bs) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((rs * 2) & 15) || ((hs * 2) & 15) ||
+      ((bs * 2) & 15))
+    return fail(ctx, LLMR_EINVAL, "TMA operand base/strides must be 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)rs * 2, (cuuint64_t)hs * 2, (cuuint64_t)bs * 2};
+  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LLMR_OK;
+}
+
+template <int D, typename OutT>
+int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
+                 const CUtensorMap &mv, int B, int H, int S, float scale, void *o,
+                 long long o_rs, long long o_bs, float *lse) {
+  using C = FaCfg<D>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    CUDA_TRY(ctx, cudaFuncSetAttribute(fa_fwd_tc_kernel<D, OutT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set = true;
+  }
+  FaParams p;
+  p.S = S;
+  p.H = H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = o;
+  p.o_row_stride = o_rs;
+  p.o_batch_stride = o_bs;
+  p.lse = lse;
+  p.err = ctx->d_err;
+  dim3 grid((S + 2 * C::BM - 1) / (2 * C::BM), B * H);
+  fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
+  return after_launch(ctx, "fa_fwd_tc");
+}
+
+int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
+                     const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S,
+                     float scale, void *o, long long o_rs, long long o_bs, float *lse) {
+  if (D == 128) {
+    if (od == LLMR_F32) return launch_fa_tc<128, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+    if (od == LLMR_F16) return launch_fa_tc<128, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+    return launch_fa_tc<128, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+  }
+  if (od == LLMR_F32) return launch_fa_tc<64, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+  if (od == LLMR_F16) return launch_fa_tc<64, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+  return launch_fa_tc<64, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+}
+
+template <int D, typename InT, typename OutT>
+int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v,
+                      const long long *qs, const long long *ks, const long long *vs,
+                      OutT *out, const ProParams &pp) {
+  View<InT> vq{static_cast<const InT *>(q), qs[0], qs[1], qs[2]};
+  View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
+  View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
+  const long long rows = 3LL * pp.B * pp.S * pp.H;
+  long long blocks = (rows + 7) / 8;
+  const long long cap = (long long)ctx->num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  prologue_kernel<D, InT, OutT><<<(unsigned)blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
+  return after_launch(ctx, "prologue");
+}
+
+template <typename OutT>
+int launch_prologue(llmr_ctx *ctx, int D, llmr_dtype in, const void *q, const void *k,
+                    const void *v, const long long *qs, const long long *ks,
+                    const long long *vs, OutT *out, const ProParams &pp) {
+#define PRO_CASE(DD, T) return launch_prologue_t<DD, T, OutT>(ctx, q, k, v, qs, ks, vs, out, pp)
+  if (D == 128) {
+    if (in == LLMR_F32) PRO_CASE(128, float);
+    if (in == LLMR_F16) PRO_CASE(128, __half);
+    PRO_CASE(128, __nv_bfloat16);
+  }
+  if (in == LLMR_F32) PRO_CASE(64, float);
+  if (in == LLMR_F16) PRO_CASE(64, __half);
+  PRO_CASE(64, __nv_bfloat16);
+#undef PRO_CASE
+}
+
+int launch_exact(llmr_ctx *ctx, int D, const float *q, const float *k, const float *v,
+                 const ExactParams &ep) {
+  const int rows_per_cta = D == 128 ? 16 : 32;
+  dim3 grid((ep.S + rows_per_cta - 1) / rows_per_cta, ep.B * ep.H);
+  if (D == 128)
+    attn_exact_f32_kernel<128><<<grid, 128, 0, ctx->stream>>>(q, k, v, ep);
+  else
+    attn_exact_f32_kernel<64><<<grid, 128, 0, ctx->stream>>>(q, k, v, ep);
+  return after_launch(ctx, "attn_exact_f32");
+}
+
+unsigned grid_for(llmr_ctx *ctx, long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  const long long cap = (long long)ctx->num_sms * 16;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+size_t dtype_size(llmr_dtype t) { return t == LLMR_F32 ? 4 : 2; }
+
+bool aligned16(const void *p, long long elems_a, long long elems_b, size_t es) {
+  return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ((elems_a * (long long)es) & 15) == 0 &&
+         ((elems_b * (long long)es) & 15) == 0;
+}
+
+int check_ctx(llmr_ctx *ctx) {
+  if (!ctx) return LLMR_EINVAL;
+  CUDA_TRY(ctx, cudaSetDevice(ctx->device));
+  return LLMR_OK;
+}
+
+// Fills default strides for a desc (elements). Order: {batch, row, head}.
+void default_strides(const llmr_attn_desc *d, uint64_t rs_in, uint64_t bs_in, uint64_t hs_in,
+                     long long *out) {
+  const long long H = d->n_heads, S = d->seq_len, D = d->head_dim;
+  long long rs, hs, bs;
+  if (d->layout == LLMR_LAYOUT_BSHD) {
+    rs = H * D;
+    hs = D;
+    bs = S * H * D;
+  } else {
+    rs = D;
+    hs = S * D;
+    bs = H * S * D;
+  }
+  out[0] = bs_in ? (long long)bs_in : bs;
+  out[1] = rs_in ? (long long)rs_in : rs;
+  out[2] = hs_in ? (long long)hs_in : hs;
+}
+
+}  // namespace
+
+extern "C" {
+
+int llmr_ctx_create(int device, size_t workspace_bytes, void *stream, llmr_ctx **out) {
+  if (!out) return LLMR_EINVAL;
+  *out = nullptr;
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) return LLMR_ENODEV;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return LLMR_ENODEV;
+  if (prop.major != 10) return LLMR_ENODEV;  // sm_100a code only
+  llmr_ctx *c = new llmr_ctx();
+  c->device = device;
+  c->num_sms = prop.multiProcessorCount;
+  if (cudaSetDevice(device) != cudaSuccess) { delete c; return LLMR_ECUDA; }
+  if (stream) {
+    c->stream = static_cast<cudaStream_t>(stream);
+  } else {
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+      delete c;
+      return LLMR_ECUDA;
+    }
+    c->own_stream = true;
+  }
+  if (cudaMalloc(&c->d_err, sizeof(int)) != cudaSuccess ||
+      cudaMemset(c->d_err, 0, sizeof(int)) != cudaSuccess) {
+    llmr_ctx_destroy(c);
+    return LLMR_ENOMEM;
+  }
+  if (workspace_bytes && cudaMalloc(&c->ws, workspace_bytes) != cudaSuccess) {
+    llmr_ctx_destroy(c);
+    return LLMR_ENOMEM;
+  }
+  c->ws_bytes = workspace_bytes;
+  *out = c;
+  return LLMR_OK;
+}
+
+int llmr_ctx_destroy(llmr_ctx *ctx) {
+  if (!ctx) return LLMR_EINVAL;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  if (ctx->ws) cudaFree(ctx->ws);
+  if (ctx->d_err) cudaFree(ctx->d_err);
+  for (cudaEvent_t &e : ctx->prof_ev)
+    if (e) cudaEventDestroy(e);
+  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+  return LLMR_OK;
+}
+
+int llmr_ctx_reserve(llmr_ctx *ctx, size_t bytes) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (bytes <= ctx->ws_bytes) return LLMR_OK;
+  CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  if (ctx->ws) cudaFree(ctx->ws);
+  ctx->ws = nullptr;
+  ctx->ws_bytes = 0;
+  if (cudaMalloc(&ctx->ws, bytes) != cudaSuccess)
+    return fail(ctx, LLMR_ENOMEM, "workspace of %zu bytes: cudaMalloc failed", bytes);
+  ctx->ws_bytes = bytes;
+  return LLMR_OK;
+}
+
+int llmr_set_stream(llmr_ctx *ctx, void *stream) {
+  if (!ctx || !stream) return LLMR_EINVAL;
+  if (ctx->own_stream) {
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamDestroy(ctx->stream);
+    ctx->own_stream = false;
+  }
+  ctx->stream = static_cast<cudaStream_t>(stream);
+  return LLMR_OK;
+}
+
+void *llmr_get_stream(llmr_ctx *ctx) { return ctx ? ctx->stream : nullptr; }
+
+const char *llmr_last_error(llmr_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+uint64_t llmr_launch_count(llmr_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+int llmr_sync(llmr_ctx *ctx) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  int h = 0;
+  CUDA_TRY(ctx, cudaMemcpy(&h, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (h) {
+    CUDA_TRY(ctx, cudaMemset(ctx->d_err, 0, sizeof(int)));
+    return fail(ctx, LLMR_ETIMEOUT, "a device-side wait exceeded its limit; results are invalid");
+  }
+  return LLMR_OK;
+}
+
+int llmr_alloc(llmr_ctx *ctx, size_t bytes, void **out) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!out) return fail(ctx, LLMR_EINVAL, "null out pointer");
+  if (cudaMalloc(out, bytes) != cudaSuccess)
+    return fail(ctx, LLMR_ENOMEM, "cudaMalloc(%zu) failed", bytes);
+  return LLMR_OK;
+}
+
+int llmr_free(llmr_ctx *ctx, void *ptr) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  CUDA_TRY(ctx, cudaFree(ptr));
+  return LLMR_OK;
+}
+
+int llmr_upload(llmr_ctx *ctx, void *dst, const void *src, size_t bytes) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  CUDA_TRY(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, ctx->stream));
+  CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  return LLMR_OK;
+}
+
+int llmr_download(llmr_ctx *ctx, void *dst, const void *src, size_t bytes) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  CUDA_TRY(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(ctx, cudaStreamSynchronize(ctx->stream));
+  return LLMR_OK;
+}
+
+size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {
+  if (!d) return 0;
+  const size_t n = (size_t)d->batch * d->n_heads * d->seq_len * d->head_dim;
+  if (d->flags & LLMR_EXACT) return 3 * n * 4;
+  if (d->in_dtype == LLMR_F16 && !(d->flags & (LLMR_NORM_Q | LLMR_NORM_K | LLMR_ROPE))) return 0;
+  return 3 * n * 2;
+}
+
+int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, const void *k,
+                         const void *v, const float *q_gain, const float *k_gain,
+                         const float *cos_t, const float *sin_t, void *o, float *lse) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!d || !q || !k || !v || !o) return fail(ctx, LLMR_EINVAL, "null argument");
+  const int B = d->batch, H = d->n_heads, S = d->seq_len, D = d->head_dim;
+  if (B < 1 || H < 1 || S < 1) return fail(ctx, LLMR_EINVAL, "batch, n_heads, seq_len must be >= 1");
+  if (D != 64 && D != 128) return fail(ctx, LLMR_EINVAL, "head_dim %d unsupported (64 or 128)", D);
+  if ((long long)B * H > 65535) return fail(ctx, LLMR_EINVAL, "batch*n_heads exceeds 65535");
+  if (d->in_dtype > LLMR_BF16 || d->out_dtype > LLMR_BF16 || d->layout > LLMR_LAYOUT_BHSD)
+    return fail(ctx, LLMR_EINVAL, "bad dtype or layout");
+  if ((d->flags & LLMR_NORM_Q) && !q_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_Q needs q_gain");
+  if ((d->flags & LLMR_NORM_K) && !k_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_K needs k_gain");
+  if ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) return fail(ctx, LLMR_EINVAL, "LLMR_ROPE needs cos/sin tables");
+  if ((d->flags & LLMR_LSE) && !lse) return fail(ctx, LLMR_EINVAL, "LLMR_LSE needs an lse buffer");
+  if (d->split_row > (uint32_t)S) return fail(ctx, LLMR_EINVAL, "split_row > seq_len");
+  const bool exact = d->flags & LLMR_EXACT;
+  if (exact && d->out_dtype != LLMR_F32) return fail(ctx, LLMR_EINVAL, "LLMR_EXACT writes fp32 output");
+  const size_t need = llmr_attention_workspace_bytes(d);
+  if (need > ctx->ws_bytes)
+    return fail(ctx, LLMR_ENOMEM, "workspace %zu bytes < %zu needed (llmr_ctx_reserve)", ctx->ws_bytes, need);
+
+  long long qs[3], ks[3], vs[3];
+  default_strides(d, d->q_row_stride, d->q_batch_stride, d->q_head_stride, qs);
+  default_strides(d, d->k_row_stride, d->k_batch_stride, d->k_head_stride, ks);
+  default_strides(d, d->v_row_stride, d->v_batch_stride, d->v_head_stride, vs);
+  const long long o_rs = d->o_row_stride ? (long long)d->o_row_stride : (long long)H * D;
+  const long long o_bs = d->o_batch_stride ? (long long)d->o_batch_stride : (long long)S * o_rs;
+  float *lse_out = (d->flags & LLMR_LSE) ? lse : nullptr;
+  if (!(d->scale > 0.0f) || !isfinite(d->scale))
+    return fail(ctx, LLMR_EINVAL, "scale must be finite and > 0");
+  if (!exact && !aligned16(o, o_rs, o_bs, dtype_size(d->out_dtype)))
+    return fail(ctx, LLMR_EINVAL, "o base, o_row_stride and o_batch_stride must be 16-byte aligned");
+
+  ProParams pp;
+  pp.B = B;
+  pp.S = S;
+  pp.H = H;
+  pp.split_row = (int)d->split_row;
+  pp.rope_row_offset = (int)d->rope_row_offset;
+  pp.eps = d->eps;
+  pp.q_gain = (d->flags & LLMR_NORM_Q) ? q_gain : nullptr;
+  pp.k_gain = (d->flags & LLMR_NORM_K) ? k_gain : nullptr;
+  pp.cos_t = (d->flags & LLMR_ROPE) ? cos_t : nullptr;
+  pp.sin_t = (d->flags & LLMR_ROPE) ? sin_t : nullptr;
+
+  const long long plane = (long long)B * H * S * D;
+  auto mark = [&](int i) {
+    if (ctx->prof_on) cudaEventRecord(ctx->prof_ev[i], ctx->stream);
+  };
+  ctx->prof_valid = false;
+  mark(0);
+  if (exact) {
+    float *w = static_cast<float *>(ctx->ws);
+    rc = launch_prologue<float>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
+    if (rc) return rc;
+    mark(1);
+    ExactParams ep;
+    ep.B = B;
+    ep.H = H;
+    ep.S = S;
+    ep.scale = d->scale;
+    ep.o = static_cast<float *>(o);
+    ep.o_batch_stride = o_bs;
+    ep.o_row_stride = o_rs;
+    ep.o_head_stride = D;
+    ep.lse = lse_out;
+    rc = launch_exact(ctx, D, w, w + plane, w + 2 * plane, ep);
+    mark(2);
+    ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
+    return rc;
+  }
+
+  CUtensorMap mq, mk, mv;
+  const bool direct = need == 0;
+  if (direct) {
+    if ((rc = make_map(ctx, &mq, q, D, S, H, B, qs[1], qs[2], qs[0]))) return rc;
+    if ((rc = make_map(ctx, &mk, k, D, S, H, B, ks[1], ks[2], ks[0]))) return rc;
+    if ((rc = make_map(ctx, &mv, v, D, S, H, B, vs[1], vs[2], vs[0]))) return rc;
+  } else {
+    __half *w = static_cast<__half *>(ctx->ws);
+    rc = launch_prologue<__half>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
+    if (rc) return rc;
+    // Workspace layout: dense [3][B][H][S][D] fp16.
+    const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
+    if ((rc = make_map(ctx, &mq, w, D, S, H, B, rs, hs, bs))) return rc;
+    if ((rc = make_map(ctx, &mk, w + plane, D, S, H, B, rs, hs, bs))) return rc;
+    if ((rc = make_map(ctx, &mv, w + 2 * plane, D, S, H, B, rs, hs, bs))) return rc;
+  }
+  mark(1);
+  rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o, o_rs, o_bs,
+                        lse_out);
+  mark(2);
+  ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
+  return rc;
+}
+
+int llmr_profile_enable(llmr_ctx *ctx, int on) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (on) {
+    for (cudaEvent_t &e : ctx->prof_ev)
+      if (!e) CUDA_TRY(ctx, cudaEventCreate(&e));
+  }
+  ctx->prof_on = on != 0;
+  ctx->prof_valid = false;
+  return LLMR_OK;
+}
+
+int llmr_profile_read(llmr_ctx *ctx, float *ms2) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!ms2) return fail(ctx, LLMR_EINVAL, "null output");
+  if (!ctx->prof_valid) return fail(ctx, LLMR_EINVAL, "no profiled call recorded");
+  CUDA_TRY(ctx, cudaEventSynchronize(ctx->prof_ev[2]));
+  CUDA_TRY(ctx, cudaEventElapsedTime(&ms2[0], ctx->prof_ev[0], ctx->prof_ev[1]));
+  CUDA_TRY(ctx, cudaEventElapsedTime(&ms2[1], ctx->prof_ev[1], ctx->prof_ev[2]));
+  return LLMR_OK;
+}
+
+int llmr_flash_attention_v2(llmr_ctx *ctx, const float *q, const float *k, const float *v,
+                            float *o, uint32_t head_dim, uint32_t n_heads, uint32_t seq_len,
+                            float scale) {
+  llmr_attn_desc d;
+  memset(&d, 0, sizeof d);
+  d.batch = 1;
+  d.n_heads = n_heads;
+  d.seq_len = seq_len;
+  d.head_dim = head_dim;
+  d.in_dtype = LLMR_F32;
+  d.out_dtype = LLMR_F32;
+  d.layout = LLMR_LAYOUT_BHSD;
+  d.scale = scale;
+  return llmr_attention_fused(ctx, &d, q, k, v, nullptr, nullptr, nullptr, nullptr, o, nullptr);
+}
+
+int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k, const float *v,
+                           float *scores, float *o, uint32_t head_dim, uint32_t n_heads,
+                           uint32_t seq_len, float scale) {
+  (void)scores;
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!q || !k || !v || !o) return fail(ctx, LLMR_EINVAL, "null argument");
+  if (head_dim != 64 && head_dim != 128)
+    return fail(ctx, LLMR_EINVAL, "head_dim %u unsupported (64 or 128)", head_dim);
+  if (n_heads < 1 || seq_len < 1 || n_heads > 65535) return fail(ctx, LLMR_EINVAL, "bad n_heads/seq_len");
+  ExactParams ep;
+  ep.B = 1;
+  ep.H = (int)n_heads;
+  ep.S = (int)seq_len;
+  ep.scale = scale;
+  ep.o = o;
+  ep.o_batch_stride = 0;
+  ep.o_row_stride = head_dim;                      // [H, S, D] output
+  ep.o_head_stride = (long long)seq_len * head_dim;
+  ep.lse = nullptr;
+  return launch_exact(ctx, (int)head_dim, q, k, v, ep);
+}
+
+int llmr_batch_head_norm(llmr_ctx *ctx, float *data, const float *gain, uint32_t n_heads,
+                         uint32_t head_dim, uint32_t seq_len, float eps) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!data || !gain || !head_dim) return fail(ctx, LLMR_EINVAL, "null argument or head_dim 0");
+  const long long rows = (long long)seq_len * n_heads;
+  if (rows == 0) return LLMR_OK;
+  head_norm_f32_kernel<<<grid_for(ctx, rows * 32, 256), 256, 0, ctx->stream>>>(
+      data, gain, (int)n_heads, (int)head_dim, (int)seq_len, eps);
+  return after_launch(ctx, "head_norm_f32");
+}
+
+int llmr_perhead_rmsnorm(llmr_ctx *ctx, float *data, const float *weight, uint32_t seq_len,
+                         uint32_t n_heads, uint32_t head_dim, float eps) {
+  return llmr_batch_head_norm(ctx, data, weight, n_heads, head_dim, seq_len, eps);
+}
+
+int llmr_transpose_heads(llmr_ctx *ctx, const float *in, float *out, uint32_t seq_len,
+                         uint32_t n_heads, uint32_t head_dim, uint32_t direction) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!in || !out || in == out) return fail(ctx, LLMR_EINVAL, "null or aliased buffers");
+  if (direction > 1) return fail(ctx, LLMR_EINVAL, "direction must be 0 or 1");
+  const long long n = (long long)seq_len * n_heads * head_dim;
+  if (n == 0) return LLMR_OK;
+  transpose_heads_kernel<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(
+      in, out, (int)seq_len, (int)n_heads, (int)head_dim, (int)direction);
+  return after_launch(ctx, "transpose_heads");
+}
+
+int llmr_mrope(llmr_ctx *ctx, float *data, const float *cos_t, const float *sin_t,
+               uint32_t seq_len, uint32_t n_heads) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!data || !cos_t || !sin_t) return fail(ctx, LLMR_EINVAL, "null argument");
+  const long long n = (long long)seq_len * n_heads * 64;
+  if (n == 0) return LLMR_OK;
+  mrope_f32_kernel<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(data, cos_t, sin_t,
+                                                                  (int)seq_len, (int)n_heads, 64);
+  return after_launch(ctx, "mrope_f32");
+}
+
+int llmr_split_qkv(llmr_ctx *ctx, const float *qkv, float *q, float *k, float *v, uint32_t dim,
+                   uint32_t n_rows) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!qkv || !q || !k || !v) return fail(ctx, LLMR_EINVAL, "null argument");
+  const long long n = (long long)n_rows * dim;
+  if (n == 0) return LLMR_OK;
+  split_qkv_kernel<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(qkv, q, k, v, (int)dim,
+                                                                  (int)n_rows);
+  return after_launch(ctx, "split_qkv");
+}
+
+int llmr_attention_merge(llmr_ctx *ctx, float *o_a, float *lse_a, const float *o_b,
+                         const float *lse_b, uint32_t rows, uint32_t n_heads, uint32_t head_dim,
+                         uint64_t o_row_stride) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!o_a || !lse_a || !o_b || !lse_b) return fail(ctx, LLMR_EINVAL, "null argument");
+  const long long rs = o_row_stride ? (long long)o_row_stride : (long long)n_heads * head_dim;
+  const long long n = (long long)rows * n_heads * head_dim;
+  if (n == 0) return LLMR_OK;
+  merge_kernel<<<grid_for(ctx, n, 256), 256, 0, ctx->stream>>>(o_a, lse_a, o_b, lse_b, (int)rows,
+                                                              (int)n_heads, (int)head_dim, rs);
+  if ((rc = after_launch(ctx, "merge"))) return rc;
+  const long long nl = (long long)rows * n_heads;
+  merge_lse_kernel<<<grid_for(ctx, nl, 256), 256, 0, ctx->stream>>>(lse_a, lse_b, nl);
+  return after_launch(ctx, "merge_lse");
+}
+
+int llmr_rope_tables(const int32_t *pos, uint32_t seq_len, uint32_t n_axes,
+                     const uint32_t *axes_dims, float theta, float *cos_out, float *sin_out) {
+  if (!pos || !axes_dims || !cos_out || !sin_out || n_axes == 0) return LLMR_EINVAL;
+  uint32_t half = 0;
+  for (uint32_t a = 0; a < n_axes; a++) {
+    if (axes_dims[a] % 2) return LLMR_EINVAL;
+    half += axes_dims[a] / 2;
+  }
+  // freq = 1/theta^(2k/d_a), angle = pos * freq, in float, as the reference
+  // host code computes them (dependencies/flux.c3l/flux_dit.c3:461-497).
+  for (uint64_t t = 0; t < seq_len; t++) {
+    uint32_t pair = 0;
+    for (uint32_t a = 0; a < n_axes; a++) {
+      const uint32_t ha = axes_dims[a] / 2;
+      for (uint32_t kk = 0; kk < ha; kk++) {
+        const float freq = 1.0f / powf(theta, (float)(2 * kk) / (float)axes_dims[a]);
+        const float angle = (float)pos[t * n_axes + a] * freq;
+        cos_out[t * half + pair] = cosf(angle);
+        sin_out[t * half + pair] = sinf(angle);
+        pair++;
+      }
+    }
+  }
+  return LLMR_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,335 @@
+"""Python host mirror of the llm-runner attention operator surface, on B200.
+
+The reference records its attention ops through `RenderGraph.dispatch`
+(lib/vulkan/graph.c3:47-72) with fp32 `llm::Tensor` bindings and a push
+constant struct per op (dependencies/zimage.c3l/dit.c3:120-170). This package
+exposes the same operators, with the same names, argument meaning and
+argument order, over the C-ABI library `libllmr_attn.so` (include/llmr_attn.h):
+
+    flash_attention_v2(ctx, q, k, v, o, head_dim, n_heads, seq_len, scale)
+    batch_head_norm(ctx, data, gain, n_heads, head_dim, seq_len, eps)
+    perhead_rmsnorm(ctx, data, weight, seq_len, n_heads, head_dim, eps)
+    transpose_heads(ctx, inp, out, seq_len, n_heads, head_dim, direction)
+    mrope(ctx, data, cos, sin, seq_len, n_heads)
+    spatial_attention(ctx, q, k, v, scores, o, head_dim, n_heads, seq_len, scale)
+    split_qkv(ctx, qkv, q, k, v, dim, n_rows)
+
+plus the fused op `attention_fused` that replaces the whole 8-dispatch
+sequence of a DiT attention block. Buffers are torch CUDA tensors (device
+memory and streams only; all compute is in the library's CUDA kernels).
+There is no CPU fallback: importing this package without the built library
+raises, and every op on a machine without an sm_100 GPU fails with
+LlmrError(LLMR_ENODEV).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libllmr_attn.so")
+
+OK, EINVAL, ENOMEM, ECUDA, ENCCL, ETIMEOUT, ENODEV = range(7)
+_STATUS_NAMES = {0: "LLMR_OK", 1: "LLMR_EINVAL", 2: "LLMR_ENOMEM", 3: "LLMR_ECUDA",
+                 4: "LLMR_ENCCL", 5: "LLMR_ETIMEOUT", 6: "LLMR_ENODEV"}
+
+F32, F16, BF16 = 0, 1, 2
+BSHD, BHSD = 0, 1
+NORM_Q, NORM_K, ROPE, EXACT, LSE = 1, 2, 4, 8, 16
+
+
+class LlmrError(RuntimeError):
+    """A non-zero status from the C ABI (the reference raises a fault)."""
+
+    def __init__(self, status: int, message: str = ""):
+        self.status = status
+        super().__init__(f"{_STATUS_NAMES.get(status, status)}: {message}")
+
+
+class AttnDesc(ctypes.Structure):
+    """Mirror of llmr_attn_desc (include/llmr_attn.h)."""
+
+    _fields_ = [
+        ("batch", ctypes.c_uint32), ("n_heads", ctypes.c_uint32),
+        ("seq_len", ctypes.c_uint32), ("head_dim", ctypes.c_uint32),
+        ("in_dtype", ctypes.c_int), ("out_dtype", ctypes.c_int),
+        ("layout", ctypes.c_int), ("flags", ctypes.c_uint32),
+        ("scale", ctypes.c_float), ("eps", ctypes.c_float),
+        ("split_row", ctypes.c_uint32), ("rope_row_offset", ctypes.c_uint32),
+        ("q_row_stride", ctypes.c_uint64), ("k_row_stride", ctypes.c_uint64),
+        ("v_row_stride", ctypes.c_uint64), ("o_row_stride", ctypes.c_uint64),
+        ("q_batch_stride", ctypes.c_uint64), ("k_batch_stride", ctypes.c_uint64),
+        ("v_batch_stride", ctypes.c_uint64), ("o_batch_stride", ctypes.c_uint64),
+        ("q_head_stride", ctypes.c_uint64), ("k_head_stride", ctypes.c_uint64),
+        ("v_head_stride", ctypes.c_uint64),
+    ]
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is not built; run `make -C llm-runner_b200/csrc` "
+            "(or __graft_entry__.build()). There is no CPU fallback.")
+    lib = ctypes.CDLL(LIB_PATH)
+    vp, u32, u64, f32, i32 = (ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint64,
+                              ctypes.c_float, ctypes.c_int)
+    sig = {
+        "llmr_ctx_create": (i32, [i32, ctypes.c_size_t, vp, ctypes.POINTER(vp)]),
+        "llmr_ctx_destroy": (i32, [vp]),
+        "llmr_ctx_reserve": (i32, [vp, ctypes.c_size_t]),
+        "llmr_set_stream": (i32, [vp, vp]),
+        "llmr_get_stream": (vp, [vp]),
+        "llmr_last_error": (ctypes.c_char_p, [vp]),
+        "llmr_sync": (i32, [vp]),
+        "llmr_launch_count": (u64, [vp]),
+        "llmr_profile_enable": (i32, [vp, i32]),
+        "llmr_profile_read": (i32, [vp, ctypes.POINTER(ctypes.c_float)]),
+        "llmr_alloc": (i32, [vp, ctypes.c_size_t, ctypes.POINTER(vp)]),
+        "llmr_free": (i32, [vp, vp]),
+        "llmr_upload": (i32, [vp, vp, vp, ctypes.c_size_t]),
+        "llmr_download": (i32, [vp, vp, vp, ctypes.c_size_t]),
+        "llmr_flash_attention_v2": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, f32]),
+        "llmr_batch_head_norm": (i32, [vp, vp, vp, u32, u32, u32, f32]),
+        "llmr_perhead_rmsnorm": (i32, [vp, vp, vp, u32, u32, u32, f32]),
+        "llmr_transpose_heads": (i32, [vp, vp, vp, u32, u32, u32, u32]),
+        "llmr_mrope": (i32, [vp, vp, vp, vp, u32, u32]),
+        "llmr_spatial_attention": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, f32]),
+        "llmr_split_qkv": (i32, [vp, vp, vp, vp, vp, u32, u32]),
+        "llmr_attention_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(AttnDesc)]),
+        "llmr_attention_fused": (i32, [vp, ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
+                                       vp, vp, vp, vp]),
+        "llmr_attention_merge": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, u64]),
+        "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+lib = _load()
+
+
+def _ptr(t) -> Optional[int]:
+    """Device (or host numpy) address of a tensor/array; None passes NULL."""
+    if t is None:
+        return None
+    if isinstance(t, np.ndarray):
+        return t.ctypes.data
+    return t.data_ptr()
+
+
+class Context:
+    """One llmr_ctx: a device, a CUDA stream, and a workspace.
+
+    By default the context runs on torch's current stream of `device`, so
+    library kernels and torch copies are ordered with each other and CUDA
+    events recorded by torch time them. Replaces createContext()
+    (lib/vulkan/context.c3:73).
+    """
+
+    def __init__(self, device: int = 0, workspace_bytes: int = 0, stream=None):
+        import torch
+        if stream is None:
+            stream = torch.cuda.current_stream(device)
+        handle = ctypes.c_void_p()
+        raw = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+        rc = lib.llmr_ctx_create(device, workspace_bytes, ctypes.c_void_p(raw),
+                                 ctypes.byref(handle))
+        if rc != OK:
+            raise LlmrError(rc, f"llmr_ctx_create(device={device})")
+        self.handle = handle
+        self.device = device
+
+    def check(self, rc: int) -> None:
+        if rc != OK:
+            msg = lib.llmr_last_error(self.handle)
+            raise LlmrError(rc, msg.decode() if msg else "")
+
+    def reserve(self, nbytes: int) -> None:
+        self.check(lib.llmr_ctx_reserve(self.handle, nbytes))
+
+    def sync(self) -> None:
+        self.check(lib.llmr_sync(self.handle))
+
+    def profile(self, on: bool = True) -> None:
+        """Per-phase CUDA-event timing of fused calls (prologue, attention)."""
+        self.check(lib.llmr_profile_enable(self.handle, 1 if on else 0))
+
+    def profile_read(self):
+        """(prologue_ms, attention_ms) of the last profiled fused call."""
+        ms = (ctypes.c_float * 2)()
+        self.check(lib.llmr_profile_read(self.handle, ms))
+        return float(ms[0]), float(ms[1])
+
+    @property
+    def launches(self) -> int:
+        return int(lib.llmr_launch_count(self.handle))
+
+    def close(self) -> None:
+        if getattr(self, "handle", None):
+            lib.llmr_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------- reference op mirrors
+
+def flash_attention_v2(ctx: Context, q, k, v, o, head_dim: int, n_heads: int,
+                       seq_len: int, scale: float) -> None:
+    """flash_attn.slang:38-241. q,k,v fp32 [H,S,D]; o fp32 [S,H*D]."""
+    ctx.check(lib.llmr_flash_attention_v2(ctx.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                          head_dim, n_heads, seq_len, scale))
+
+
+def batch_head_norm(ctx: Context, data, gain, n_heads: int, head_dim: int,
+                    seq_len: int, eps: float) -> None:
+    """zimage.slang:623-659, in place on fp32 [S,H*D]."""
+    ctx.check(lib.llmr_batch_head_norm(ctx.handle, _ptr(data), _ptr(gain), n_heads,
+                                       head_dim, seq_len, eps))
+
+
+def perhead_rmsnorm(ctx: Context, data, weight, seq_len: int, n_heads: int,
+                    head_dim: int, eps: float) -> None:
+    """vit.slang:590-616, in place on fp32 [S,H*D]."""
+    ctx.check(lib.llmr_perhead_rmsnorm(ctx.handle, _ptr(data), _ptr(weight), seq_len,
+                                       n_heads, head_dim, eps))
+
+
+def transpose_heads(ctx: Context, inp, out, seq_len: int, n_heads: int,
+                    head_dim: int, direction: int) -> None:
+    """zimage.slang:575-601: 0 = [S,H,D]->[H,S,D], 1 = reverse."""
+    ctx.check(lib.llmr_transpose_heads(ctx.handle, _ptr(inp), _ptr(out), seq_len,
+                                       n_heads, head_dim, direction))
+
+
+def mrope(ctx: Context, data, cos, sin, seq_len: int, n_heads: int) -> None:
+    """mrope.slang:33-54, in place on fp32 [H,S,128] with tables [S,64]."""
+    ctx.check(lib.llmr_mrope(ctx.handle, _ptr(data), _ptr(cos), _ptr(sin), seq_len,
+                             n_heads))
+
+
+def spatial_attention(ctx: Context, q, k, v, scores, o, head_dim: int, n_heads: int,
+                      seq_len: int, scale: float) -> None:
+    """diffusion.slang:478-569; `scores` is accepted and ignored (may be None)."""
+    ctx.check(lib.llmr_spatial_attention(ctx.handle, _ptr(q), _ptr(k), _ptr(v),
+                                         _ptr(scores), _ptr(o), head_dim, n_heads,
+                                         seq_len, scale))
+
+
+def split_qkv(ctx: Context, qkv, q, k, v, dim: int, n_rows: int) -> None:
+    """depth.slang:40-58."""
+    ctx.check(lib.llmr_split_qkv(ctx.handle, _ptr(qkv), _ptr(q), _ptr(k), _ptr(v), dim,
+                                 n_rows))
+
+
+# ------------------------------------------------------------------------ fused op
+
+_TORCH_DTYPE_CODE = None
+
+
+def _dtype_code(t) -> int:
+    import torch
+    table = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+    if t.dtype not in table:
+        raise LlmrError(EINVAL, f"unsupported dtype {t.dtype}")
+    return table[t.dtype]
+
+
+@dataclass
+class AttnConfig:
+    """Per-call parameters of the fused op (the push constants of the eight
+    reference dispatches folded together)."""
+
+    n_heads: int
+    head_dim: int
+    scale: float
+    layout: int = BSHD
+    eps: float = 1e-6
+    norm_q: bool = False
+    norm_k: bool = False
+    rope: bool = False
+    exact: bool = False
+    split_row: int = 0
+    rope_row_offset: int = 0
+
+
+def make_desc(cfg: AttnConfig, batch: int, seq_len: int, in_dtype: int, out_dtype: int,
+              lse: bool = False, strides: Optional[dict] = None) -> AttnDesc:
+    d = AttnDesc()
+    d.batch, d.n_heads, d.seq_len, d.head_dim = batch, cfg.n_heads, seq_len, cfg.head_dim
+    d.in_dtype, d.out_dtype, d.layout = in_dtype, out_dtype, cfg.layout
+    d.flags = ((NORM_Q if cfg.norm_q else 0) | (NORM_K if cfg.norm_k else 0)
+               | (ROPE if cfg.rope else 0) | (EXACT if cfg.exact else 0)
+               | (LSE if lse else 0))
+    d.scale, d.eps = cfg.scale, cfg.eps
+    d.split_row, d.rope_row_offset = cfg.split_row, cfg.rope_row_offset
+    for key, val in (strides or {}).items():
+        setattr(d, key, int(val))
+    return d
+
+
+def workspace_bytes(desc: AttnDesc) -> int:
+    return int(lib.llmr_attention_workspace_bytes(ctypes.byref(desc)))
+
+
+def attention_fused(ctx: Context, q, k, v, o, cfg: AttnConfig, *, batch: int, seq_len: int,
+                    q_gain=None, k_gain=None, cos=None, sin=None, lse=None,
+                    strides: Optional[dict] = None) -> None:
+    """Fused QK-RMSNorm + RoPE + non-causal attention into `o` [B,S,H*D].
+
+    q/k/v: torch CUDA tensors (f32/f16/bf16) in cfg.layout; gains fp32
+    [D] or [2,D] (txt/img split at cfg.split_row); cos/sin fp32 [rows, D/2].
+    """
+    desc = make_desc(cfg, batch, seq_len, _dtype_code(q), _dtype_code(o),
+                     lse=lse is not None, strides=strides)
+    ctx.check(lib.llmr_attention_fused(ctx.handle, ctypes.byref(desc), _ptr(q), _ptr(k),
+                                       _ptr(v), _ptr(q_gain), _ptr(k_gain), _ptr(cos),
+                                       _ptr(sin), _ptr(o), _ptr(lse)))
+
+
+def attention_merge(ctx: Context, o_a, lse_a, o_b, lse_b, rows: int, n_heads: int,
+                    head_dim: int, o_row_stride: int = 0) -> None:
+    """(o_a, lse_a) <- LSE-merge of two partial results over disjoint keys."""
+    ctx.check(lib.llmr_attention_merge(ctx.handle, _ptr(o_a), _ptr(lse_a), _ptr(o_b),
+                                       _ptr(lse_b), rows, n_heads, head_dim, o_row_stride))
+
+
+# ------------------------------------------------------------------- host helpers
+
+def rope_tables(pos: np.ndarray, axes_dims: Sequence[int], theta: float):
+    """Multi-axis RoPE tables (flux_dit.c3:396-525, dit.c3:561-757), on the host.
+
+    pos: int32 [S, n_axes]. Returns (cos, sin) float32 [S, sum(axes)/2].
+    """
+    pos = np.ascontiguousarray(pos, dtype=np.int32)
+    axes = np.ascontiguousarray(axes_dims, dtype=np.uint32)
+    S, n_axes = pos.shape
+    if n_axes != len(axes):
+        raise LlmrError(EINVAL, "pos columns != number of axes")
+    half = int(axes.sum()) // 2
+    cos = np.empty((S, half), np.float32)
+    sin = np.empty((S, half), np.float32)
+    rc = lib.llmr_rope_tables(pos.ctypes.data, S, n_axes, axes.ctypes.data, theta,
+                              cos.ctypes.data, sin.ctypes.data)
+    if rc != OK:
+        raise LlmrError(rc, "llmr_rope_tables")
+    return cos, sin
+
+
+__all__ = [
+    "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
+    "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
+    "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
+    "rope_tables", "LIB_PATH", "lib",
+]

@@ -1,0 +1,339 @@
+"""GPU parity: the CUDA path (through the C ABI) against the CPU oracle and
+the golden vectors. Tolerances are the north star's: on O, max-abs <= 2e-3 and
+mean-abs <= 2e-4 for fp16/bf16 operands, <= 1e-5 for the fp32 config."""
+import numpy as np
+import pytest
+
+import oracle as O
+from conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+TOL_MAX, TOL_MEAN = 2e-3, 2e-4
+
+
+def _t():
+    import torch
+    return torch
+
+
+def dev(a):
+    return _t().from_numpy(np.ascontiguousarray(a, np.float32)).cuda()
+
+
+def host(t):
+    return t.float().cpu().numpy()
+
+
+def check(got, want, tol_max=TOL_MAX, tol_mean=TOL_MEAN, what=""):
+    assert got.shape == want.shape, (got.shape, want.shape)
+    assert np.all(np.isfinite(got)), what + ": non-finite output"
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert err.max() <= tol_max and err.mean() <= tol_mean, \
+        f"{what}: max {err.max():.3e} mean {err.mean():.3e}"
+
+
+# ----------------------------------------------------------- reference op mirrors
+
+def test_head_norm_mirror(ctx, manifest):
+    import llmr_attn as L
+    m = manifest["head_norm"]
+    p = m["params"]
+    x = dev(load_golden(m["x"]))
+    L.batch_head_norm(ctx, x, dev(load_golden(m["gain"])), p["H"], p["D"], p["S"], p["eps"])
+    ctx.sync()
+    check(host(x), load_golden(m["out"]), 1e-5, 1e-6, "batch_head_norm")
+    y = dev(load_golden(m["x"]))
+    L.perhead_rmsnorm(ctx, y, dev(load_golden(m["gain"])), p["S"], p["H"], p["D"], p["eps"])
+    ctx.sync()
+    check(host(y), load_golden(m["out"]), 1e-5, 1e-6, "perhead_rmsnorm")
+
+
+@pytest.mark.parametrize("direction", [0, 1])
+def test_transpose_mirror(ctx, manifest, direction):
+    import llmr_attn as L
+    m = manifest["transpose"]
+    p = m["params"]
+    x = dev(load_golden(m["x"]))
+    out = _t().empty_like(x)
+    L.transpose_heads(ctx, x, out, p["S"], p["H"], p["D"], direction)
+    ctx.sync()
+    np.testing.assert_array_equal(host(out).reshape(-1),
+                                  load_golden(m[f"out{direction}"]).reshape(-1))
+
+
+def test_mrope_mirror(ctx, manifest):
+    import llmr_attn as L
+    m = manifest["mrope"]
+    p = m["params"]
+    x = dev(load_golden(m["x"]))
+    L.mrope(ctx, x, dev(load_golden(m["cos"])), dev(load_golden(m["sin"])), p["S"], p["H"])
+    ctx.sync()
+    check(host(x), load_golden(m["out"]), 1e-6, 1e-7, "mrope")
+
+
+def test_split_qkv_mirror(ctx, manifest):
+    import llmr_attn as L
+    m = manifest["split_qkv"]
+    p = m["params"]
+    qkv = dev(load_golden(m["qkv"]))
+    q, k, v = (_t().empty((p["n_rows"], p["dim"]), device="cuda") for _ in range(3))
+    L.split_qkv(ctx, qkv, q, k, v, p["dim"], p["n_rows"])
+    ctx.sync()
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        np.testing.assert_array_equal(host(t), load_golden(m[name]))
+
+
+def test_flash_attention_v2_mirror(ctx, manifest):
+    import llmr_attn as L
+    m = manifest["fa2"]
+    p = m["params"]
+    ctx.reserve(3 * p["H"] * p["S"] * p["D"] * 2)
+    o = _t().empty((p["S"], p["H"] * p["D"]), device="cuda")
+    L.flash_attention_v2(ctx, dev(load_golden(m["q"])), dev(load_golden(m["k"])),
+                         dev(load_golden(m["v"])), o, p["D"], p["H"], p["S"], p["scale"])
+    ctx.sync()
+    check(host(o), load_golden(m["out"]), what="flash_attention_v2")
+
+
+def test_spatial_attention_mirror(ctx, manifest):
+    import llmr_attn as L
+    m = manifest["spatial"]
+    p = m["params"]
+    o = _t().empty((p["H"], p["S"], p["D"]), device="cuda")
+    L.spatial_attention(ctx, dev(load_golden(m["q"])), dev(load_golden(m["k"])),
+                        dev(load_golden(m["v"])), None, o, p["D"], p["H"], p["S"], p["scale"])
+    ctx.sync()
+    check(host(o), load_golden(m["out"]), 1e-5, 1e-5, "spatial_attention")
+
+
+def test_fused_block_golden(ctx, manifest):
+    """The fused op replaces the whole Flux block sequence of the fixture."""
+    import llmr_attn as L
+    m = manifest["block_flux"]
+    p = m["params"]
+    S, H, D = p["S"], p["H"], p["D"]
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=p["scale"], eps=p["eps"], norm_q=True,
+                       norm_k=True, rope=True, split_row=p["split"])
+    ctx.reserve(3 * S * H * D * 2)
+    o = _t().empty((1, S, H * D), device="cuda")
+    L.attention_fused(ctx, dev(load_golden(m["q"])), dev(load_golden(m["k"])),
+                      dev(load_golden(m["v"])), o, cfg, batch=1, seq_len=S,
+                      q_gain=dev(load_golden(m["q_gain"])), k_gain=dev(load_golden(m["k_gain"])),
+                      cos=dev(load_golden(m["cos"])), sin=dev(load_golden(m["sin"])))
+    ctx.sync()
+    check(host(o)[0], load_golden(m["out"]), what="fused block")
+
+
+# ------------------------------------------------------------- tensor-core kernel
+
+def oracle_fa(q_bshd, k_bshd, v_bshd, scale, rows=None):
+    """Reference flash_attention_v2 on BSHD inputs -> O [B,S,H*D]."""
+    B, S, H, D = q_bshd.shape
+    out = []
+    for b in range(B):
+        tr = lambda a: np.ascontiguousarray(a[b].transpose(1, 0, 2))
+        qb = None if rows is None else (rows[0] // 16, (rows[1] + 15) // 16)
+        out.append(O.flash_attention_v2(tr(q_bshd), tr(k_bshd), tr(v_bshd), D, H, S, scale,
+                                        qb_range=qb))
+    return np.stack(out)
+
+
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("S", [1, 15, 17, 33, 127, 128, 129, 255, 256, 257, 300, 1000])
+def test_tc_kernel_ragged_shapes(ctx, D, S):
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(S * 7 + D)
+    B, H = 2, 3
+    q, k, v = (rng.standard_normal((B, S, H, D), dtype=np.float32) for _ in range(3))
+    q, k, v = (a.astype(np.float16).astype(np.float32) for a in (q, k, v))
+    scale = D ** -0.5
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=scale)
+    o = torch.empty((B, S, H * D), device="cuda", dtype=torch.float32)
+    L.attention_fused(ctx, dev(q).half(), dev(k).half(), dev(v).half(), o, cfg, batch=B,
+                      seq_len=S)
+    ctx.sync()
+    check(host(o), oracle_fa(q, k, v, scale).reshape(B, S, H * D), what=f"S={S} D={D}")
+
+
+@pytest.mark.parametrize("in_dt", ["f32", "f16", "bf16"])
+@pytest.mark.parametrize("out_dt", ["f32", "f16", "bf16"])
+def test_tc_kernel_dtypes(ctx, in_dt, out_dt):
+    import llmr_attn as L
+    from llmr_attn.configs import round_to
+    from llmr_attn.runner import torch_dtype
+    torch = _t()
+    rng = np.random.default_rng(3)
+    B, S, H, D = 1, 333, 2, 128
+    q, k, v = (round_to(rng.standard_normal((B, S, H, D), dtype=np.float32), in_dt)
+               for _ in range(3))
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=D ** -0.5)
+    ctx.reserve(3 * B * S * H * D * 2)
+    o = torch.empty((B, S, H * D), device="cuda", dtype=torch_dtype(out_dt))
+    td = torch_dtype(in_dt)
+    L.attention_fused(ctx, dev(q).to(td), dev(k).to(td), dev(v).to(td), o, cfg, batch=B,
+                      seq_len=S)
+    ctx.sync()
+    want = oracle_fa(q, k, v, D ** -0.5).reshape(B, S, H * D)
+    want = round_to(want, out_dt)
+    # fp16/bf16 output adds one output rounding (<= 2^-9 relative for bf16).
+    tmax = TOL_MAX if out_dt != "bf16" else 2e-3 + 4e-3
+    check(host(o), want, tmax, 1e-3 if out_dt == "bf16" else TOL_MEAN, f"{in_dt}->{out_dt}")
+
+
+def test_tc_kernel_bhsd_and_fused_qkv_strides(ctx):
+    """BHSD layout, and a fused QKV buffer [S, 3*H*D] addressed by strides
+    (replaces split_qkv, depth.slang:40-58)."""
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(4)
+    B, S, H, D = 1, 200, 4, 64
+    qkv = rng.standard_normal((B, S, 3, H, D), dtype=np.float32).astype(np.float16)
+    qkv_d = torch.from_numpy(qkv).cuda()
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=0.125)
+    o = torch.empty((B, S, H * D), device="cuda")
+    st = {"q_row_stride": 3 * H * D, "k_row_stride": 3 * H * D, "v_row_stride": 3 * H * D,
+          "q_batch_stride": S * 3 * H * D, "k_batch_stride": S * 3 * H * D,
+          "v_batch_stride": S * 3 * H * D}
+    flat = qkv_d.view(-1)
+    L.attention_fused(ctx, flat[0:], flat[H * D:], flat[2 * H * D:], o, cfg, batch=B,
+                      seq_len=S, strides=st)
+    ctx.sync()
+    q, k, v = (qkv[:, :, i].astype(np.float32) for i in range(3))
+    want = oracle_fa(q, k, v, 0.125).reshape(B, S, H * D)
+    check(host(o), want, what="fused-qkv strides")
+    # BHSD input
+    qh, kh, vh = (torch.from_numpy(np.ascontiguousarray(a.transpose(0, 2, 1, 3))).cuda().half()
+                  for a in (q, k, v))
+    cfg2 = L.AttnConfig(n_heads=H, head_dim=D, scale=0.125, layout=L.BHSD)
+    o2 = torch.empty_like(o)
+    L.attention_fused(ctx, qh, kh, vh, o2, cfg2, batch=B, seq_len=S)
+    ctx.sync()
+    check(host(o2), want, what="bhsd")
+
+
+def test_fused_norm_rope_vs_oracle(ctx):
+    """Norm with a txt/img gain split, RoPE from host tables, bf16 inputs."""
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import to_device
+    prep = C.prepare(C.C3, L.rope_tables, seq_len=700, n_heads=3)
+    dc = to_device(prep)
+    ctx.reserve(L.workspace_bytes(dc.desc()))
+    dc.run(ctx)
+    ctx.sync()
+    want = O.attention_block(prep.q[0], prep.k[0], prep.v[0], 3, 128, C.C3.scale, eps=C.C3.eps,
+                             q_gain=prep.q_gain, k_gain=prep.k_gain, split_row=512,
+                             cos=prep.cos, sin=prep.sin)
+    check(host(dc.o)[0], C.round_to(want, "bf16"), TOL_MAX + 4e-3, 1e-3, "fused norm+rope")
+    # the same call with an fp32 output is held to the plain tolerance
+    dc.o = _t().empty(dc.o.shape, device="cuda", dtype=_t().float32)
+    dc.run(ctx)
+    ctx.sync()
+    check(host(dc.o)[0], want, what="fused norm+rope f32 out")
+
+
+def test_lse_output(ctx):
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(8)
+    B, S, H, D = 1, 390, 2, 128
+    q, k, v = (rng.standard_normal((B, S, H, D), dtype=np.float32).astype(np.float16)
+               .astype(np.float32) for _ in range(3))
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=D ** -0.5)
+    o = torch.empty((B, S, H * D), device="cuda")
+    lse = torch.empty((B, H, S), device="cuda")
+    L.attention_fused(ctx, dev(q).half(), dev(k).half(), dev(v).half(), o, cfg, batch=B,
+                      seq_len=S, lse=lse)
+    ctx.sync()
+    s = np.einsum("shd,thd->hst", q[0].astype(np.float64), k[0].astype(np.float64)) * D ** -0.5
+    mx = s.max(-1, keepdims=True)
+    want = (mx + np.log(np.exp(s - mx).sum(-1, keepdims=True)))[..., 0]
+    assert np.abs(host(lse)[0] - want).max() < 1e-3
+
+
+# ----------------------------------------------------------------- configurations
+
+def _run_case(ctx, case, rows_windows=None, **over):
+    """Runs a configuration with an fp32 output (so the strict tolerance
+    applies to the arithmetic) and compares windows of rows with the oracle."""
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import to_device
+    prep = C.prepare(case, L.rope_tables, **over)
+    dc = to_device(prep, out_dtype="f32")
+    ctx.reserve(L.workspace_bytes(dc.desc()))
+    dc.run(ctx)
+    ctx.sync()
+    got = host(dc.o)
+    B, S, H, D = prep.q.shape
+    split = min(case.split_row, S)
+    for b in range(B):
+        for (r0, r1) in (rows_windows or [(0, S)]):
+            want = O.attention_block(prep.q[b], prep.k[b], prep.v[b], H, D, case.scale,
+                                     eps=case.eps, q_gain=prep.q_gain, k_gain=prep.k_gain,
+                                     split_row=split, cos=prep.cos, sin=prep.sin,
+                                     exact=case.exact, rows=(r0, r1))
+            check(got[b, r0:r1], want[r0:r1], case.tol_max, case.tol_mean,
+                  f"{case.name} b={b} rows {r0}:{r1}")
+    return dc, prep, got
+
+
+def test_config_plumbing_fp32_exact(ctx):
+    from llmr_attn import configs as C
+    _run_case(ctx, C.C1)
+
+
+def test_config_depth_fp16(ctx):
+    from llmr_attn import configs as C
+    _run_case(ctx, C.C2)
+
+
+def test_config_flux_bf16_full(ctx):
+    from llmr_attn import configs as C
+    from llmr_attn.configs import round_to
+    dc, prep, got = _run_case(ctx, C.C3)
+    # The bf16 output of the same call is the RNE rounding of the fp32 one.
+    dc.o = _t().empty(dc.o.shape, device="cuda", dtype=_t().bfloat16)
+    dc.run(ctx)
+    ctx.sync()
+    np.testing.assert_array_equal(host(dc.o), round_to(got, "bf16"))
+
+
+def test_config_zimage_cfg_sampled(ctx):
+    from llmr_attn import configs as C
+    S = C.C4.seq_len
+    _run_case(ctx, C.C4, rows_windows=[(0, 64), (256, 320), (S - 48, S)])
+
+
+def test_config_qwen_long_sampled(ctx):
+    from llmr_attn import configs as C
+    S = C.C5.seq_len
+    _run_case(ctx, C.C5, rows_windows=[(1008, 1072), (S - 32, S)])
+
+
+# ------------------------------------------------------------------ error behaviour
+
+def test_errors_are_reported(ctx):
+    import llmr_attn as L
+    torch = _t()
+    x = torch.zeros((1, 16, 2, 96), device="cuda", dtype=torch.float16)
+    o = torch.zeros((1, 16, 192), device="cuda", dtype=torch.float16)
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_fused(ctx, x, x, x, o, L.AttnConfig(n_heads=2, head_dim=96, scale=0.1),
+                          batch=1, seq_len=16)
+    assert ei.value.status == L.EINVAL and "head_dim" in str(ei.value)
+    big = torch.zeros((1, 16, 2, 128), device="cuda", dtype=torch.bfloat16)
+    ob = torch.zeros((1, 16, 256), device="cuda", dtype=torch.bfloat16)
+    tiny = L.Context(0, workspace_bytes=64)
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_fused(tiny, big, big, big, ob, L.AttnConfig(n_heads=2, head_dim=128,
+                                                                scale=0.1),
+                          batch=1, seq_len=16)
+    assert ei.value.status == L.ENOMEM
+    tiny.close()
+    with pytest.raises(L.LlmrError):
+        L.attention_fused(ctx, big, big, big, ob, L.AttnConfig(n_heads=2, head_dim=128,
+                                                               scale=-1.0), batch=1, seq_len=16)
+    ctx.sync()
