@@ -67,7 +67,8 @@ enum {
 typedef struct llmr_ctx llmr_ctx;
 
 /* Create a context on CUDA device `device`, using `stream` (a cudaStream_t;
- * NULL = a new non-blocking stream owned by the context) and a device
+ * NULL = a new non-blocking stream owned by the context; pass
+ * cudaStreamLegacy to run on the legacy default stream) and a device
  * workspace of `workspace_bytes` (may be 0 and grown by llmr_ctx_reserve).
  * Replaces createContext() (lib/vulkan/context.c3:73). */
 int llmr_ctx_create(int device, size_t workspace_bytes, void *stream,
@@ -175,11 +176,14 @@ typedef struct {
   uint32_t flags;                             /* LLMR_NORM_Q | ... */
   float scale;                                /* softmax scale */
   float eps;                                  /* RMSNorm epsilon */
-  /* Rows [0, split_row) use gain set 0, rows [split_row, S) gain set 1
-   * (txt/img gains, flux_dit.c3:812-845). q_gain/k_gain point to 2*head_dim
-   * fp32 device values when split_row > 0, else head_dim values. */
+  /* Tokens with global index < split_row use gain set 0, the others gain
+   * set 1 (txt/img gains, flux_dit.c3:812-845). q_gain/k_gain point to
+   * 2*head_dim fp32 device values when split_row > 0, else head_dim values.
+   * The global index of token s is rope_row_offset + s. */
   uint32_t split_row;
-  /* Row of the cos/sin tables that token 0 uses (sequence shards). */
+  /* Global index of token 0: the cos/sin table row it uses and its position
+   * against split_row (0 for a whole sequence; the shard start for a
+   * sequence shard). */
   uint32_t rope_row_offset;
   /* Element strides; 0 = dense default. */
   uint64_t q_row_stride, k_row_stride, v_row_stride, o_row_stride;

@@ -157,10 +157,24 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
   const long long rows = 3LL * pp.B * pp.S * pp.H;
-  long long blocks = (rows + 7) / 8;
-  const long long cap = (long long)ctx->num_sms * 8;
+  long long blocks = (rows + 31) / 32;  // 8 warps x 4 rows per block
+  const long long cap = (long long)ctx->num_sms * 16;
   if (blocks > cap) blocks = cap;
-  prologue_kernel<D, InT, OutT><<<(unsigned)blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
+  // One vector access per lane needs every lane's first element aligned to
+  // E elements: bases aligned and strides multiples of E; tables likewise.
+  constexpr int E = D / 32;
+  auto ok = [&](const void *ptr, const long long *st, size_t bytes) {
+    return ptr == nullptr ||
+           ((reinterpret_cast<uintptr_t>(ptr) % bytes) == 0 &&
+            (st == nullptr || (st[0] % E == 0 && st[1] % E == 0 && st[2] % E == 0)));
+  };
+  const bool vec = ok(q, qs, sizeof(InT) * E) && ok(k, ks, sizeof(InT) * E) &&
+                   ok(v, vs, sizeof(InT) * E) && ok(pp.cos_t, nullptr, 4 * (E / 2)) &&
+                   ok(pp.sin_t, nullptr, 4 * (E / 2));
+  if (vec)
+    prologue_kernel<D, InT, OutT, true><<<(unsigned)blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
+  else
+    prologue_kernel<D, InT, OutT, false><<<(unsigned)blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   return after_launch(ctx, "prologue");
 }
 
@@ -383,7 +397,6 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
   if ((d->flags & LLMR_NORM_K) && !k_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_K needs k_gain");
   if ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) return fail(ctx, LLMR_EINVAL, "LLMR_ROPE needs cos/sin tables");
   if ((d->flags & LLMR_LSE) && !lse) return fail(ctx, LLMR_EINVAL, "LLMR_LSE needs an lse buffer");
-  if (d->split_row > (uint32_t)S) return fail(ctx, LLMR_EINVAL, "split_row > seq_len");
   const bool exact = d->flags & LLMR_EXACT;
   if (exact && d->out_dtype != LLMR_F32) return fail(ctx, LLMR_EINVAL, "LLMR_EXACT writes fp32 output");
   const size_t need = llmr_attention_workspace_bytes(d);

@@ -139,6 +139,11 @@ class Context:
             stream = torch.cuda.current_stream(device)
         handle = ctypes.c_void_p()
         raw = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+        if not raw:
+            # torch's default stream is the legacy default stream (handle 0);
+            # name it explicitly (cudaStreamLegacy) so that the library does
+            # not create a stream of its own.
+            raw = 1
         rc = lib.llmr_ctx_create(device, workspace_bytes, ctypes.c_void_p(raw),
                                  ctypes.byref(handle))
         if rc != OK:
