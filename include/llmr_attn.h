@@ -203,6 +203,31 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *desc,
                          const float *cos_t, const float *sin_t, void *o,
                          float *lse);
 
+/* Allocation-free variant of llmr_attention_fused (tensor-core path only).
+ * It has no counterpart in the reference. It is for callers that cannot
+ * allocate device memory: those whose HBM belongs to another allocator (a
+ * serving runtime or host engine that reserves memory up front and accounts
+ * for every byte) and latency-critical paths that must not call
+ * cudaMalloc/cudaFree, which can synchronise the whole device. Such callers
+ * cannot create an llmr_ctx, so this call takes a cudaStream_t (NULL = the
+ * default stream) and runs on the current device.
+ *  - Scratch: a fixed array inside the library, LLMR_NOALLOC_SCRATCH_BYTES
+ *    per GPU that loads the library, held until the process exits. Calls
+ *    needing more (3*B*H*S*D*2 bytes, when a prologue runs) return
+ *    LLMR_ENOMEM; fp16 input without norm/RoPE needs none.
+ *  - The first call on each device looks up the scratch address; make that
+ *    first call before any stream capture.
+ *  - All calls share the scratch: calls that overlap on the GPU race.
+ *  - LLMR_EXACT is rejected (LLMR_EINVAL). The call does not synchronise and
+ *    does not report device-side timeouts.
+ * Returns a status code only (there is no context for a message). */
+#define LLMR_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
+int llmr_attention_fused_noalloc(const llmr_attn_desc *desc, const void *q,
+                                 const void *k, const void *v,
+                                 const float *q_gain, const float *k_gain,
+                                 const float *cos_t, const float *sin_t,
+                                 void *o, float *lse, void *stream);
+
 /* Merge two normalised partial attention results over disjoint key sets
  * (o_a, lse_a) and (o_b, lse_b) into (o_a, lse_a): the combine step of the
  * sequence-sharded ring. o_*: fp32 [rows][n_heads*head_dim] (row stride

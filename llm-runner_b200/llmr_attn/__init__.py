@@ -103,6 +103,8 @@ def _load() -> ctypes.CDLL:
         "llmr_attention_fused": (i32, [vp, ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp]),
         "llmr_attention_merge": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, u64]),
+        "llmr_attention_fused_noalloc": (i32, [ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
+                                               vp, vp, vp, vp, vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
     }
     for name, (res, args) in sig.items():
@@ -301,6 +303,30 @@ def attention_fused(ctx: Context, q, k, v, o, cfg: AttnConfig, *, batch: int, se
     ctx.check(lib.llmr_attention_fused(ctx.handle, ctypes.byref(desc), _ptr(q), _ptr(k),
                                        _ptr(v), _ptr(q_gain), _ptr(k_gain), _ptr(cos),
                                        _ptr(sin), _ptr(o), _ptr(lse)))
+
+
+NOALLOC_SCRATCH_BYTES = 64 << 20
+
+
+def attention_fused_noalloc(q, k, v, o, cfg: AttnConfig, *, batch: int, seq_len: int,
+                            q_gain=None, k_gain=None, cos=None, sin=None, lse=None,
+                            strides: Optional[dict] = None, stream=None) -> None:
+    """The allocation-free fused op (llmr_attention_fused_noalloc): no
+    context, no device allocation; scratch is a fixed array inside the
+    library (NOALLOC_SCRATCH_BYTES per GPU). For callers whose device memory
+    is owned by another allocator or who must not call cudaMalloc/cudaFree.
+    Runs on the current device, on `stream` (default: torch's current)."""
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    raw = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+    desc = make_desc(cfg, batch, seq_len, _dtype_code(q), _dtype_code(o),
+                     lse=lse is not None, strides=strides)
+    rc = lib.llmr_attention_fused_noalloc(ctypes.byref(desc), _ptr(q), _ptr(k), _ptr(v),
+                                          _ptr(q_gain), _ptr(k_gain), _ptr(cos), _ptr(sin),
+                                          _ptr(o), _ptr(lse), ctypes.c_void_p(raw or None))
+    if rc != OK:
+        raise LlmrError(rc, "llmr_attention_fused_noalloc")
 
 
 def attention_merge(ctx: Context, o_a, lse_a, o_b, lse_b, rows: int, n_heads: int,
