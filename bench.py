@@ -38,7 +38,32 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="flux_1024")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-run", action="store_true",
+                    help="only W + K fused calls, nothing else (for ncu captures)")
+    ap.add_argument("--heads", type=int, default=0,
+                    help="with --profile-run: use this many heads (a smaller capture)")
     return ap.parse_args()
+
+
+def profile_run(args):
+    """Exactly W + K fused calls of the configuration on cuda:0 and nothing
+    else, so that an ncu launch list or capture sees only the op's kernels."""
+    import torch
+
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import to_device
+    case = C.CASES[args.config]
+    prep = C.prepare(case, L.rope_tables, n_heads=args.heads or None)
+    dc = to_device(prep)
+    ctx = L.Context(0)
+    ctx.reserve(L.workspace_bytes(dc.desc()))
+    for _ in range(args.warmup + args.steps):
+        dc.run(ctx)
+    ctx.sync()
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_run": case.name, "heads": dc.cfg.n_heads,
+                      "calls": args.warmup + args.steps, "launches": ctx.launches}))
 
 
 def peaks():
@@ -176,6 +201,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.profile_run:
+        profile_run(args)
         return
     import numpy as np
     import torch

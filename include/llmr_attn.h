@@ -228,6 +228,24 @@ int llmr_attention_fused_noalloc(const llmr_attn_desc *desc, const void *q,
                                  const float *cos_t, const float *sin_t,
                                  void *o, float *lse, void *stream);
 
+/* The prologue of llmr_attention_fused on its own: per-head RMSNorm and RoPE
+ * of Q and K, cast of V, written as dense fp16 [3][B][H][S][D] to `qkv_out`
+ * (Q at 0, K at B*H*S*D, V at 2*B*H*S*D elements; 16-byte aligned). The
+ * sequence-sharded ring runs it once per shard (rope_row_offset = shard
+ * start) and then moves the fp16 K/V block between GPUs. Replaces the
+ * batch_head_norm / transpose_heads / mrope dispatches of a block
+ * (dependencies/flux.c3l/flux_dit.c3:812-863). LLMR_EXACT is rejected. */
+int llmr_attention_prologue(llmr_ctx *ctx, const llmr_attn_desc *desc,
+                            const void *q, const void *k, const void *v,
+                            const float *q_gain, const float *k_gain,
+                            const float *cos_t, const float *sin_t,
+                            void *qkv_out);
+
+/* dst[i] = (dtype) src[i] for n fp32 values (RNE), e.g. the merged fp32
+ * output of the ring into the model's bf16 activations. */
+int llmr_convert_f32(llmr_ctx *ctx, const float *src, void *dst,
+                     llmr_dtype dst_dtype, size_t n);
+
 /* Merge two normalised partial attention results over disjoint key sets
  * (o_a, lse_a) and (o_b, lse_b) into (o_a, lse_a): the combine step of the
  * sequence-sharded ring. o_*: fp32 [rows][n_heads*head_dim] (row stride

@@ -60,6 +60,16 @@ __device__ __forceinline__ void reg_fence32(uint32_t *r) {
 #pragma unroll
   for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
 }
+__device__ __forceinline__ void reg_fence16(uint32_t *r) {
+#pragma unroll
+  for (int i = 0; i < 16; i++) asm volatile("" : "+r"(r[i]));
+}
+
+// Compile-time chunk index for the softmax's chunk loops.
+template <int N>
+struct Chunk {
+  static constexpr int value = N;
+};
 
 template <typename OutT>
 __device__ __forceinline__ void store_row_chunk(OutT *dst, const float *v);
@@ -277,66 +287,108 @@ __global__ void __launch_bounds__(320, 1)
       if (!ok) break;
       tc_fence_after();
       const int valid = S - j * C::BN;  // keys of this block below seq_len
-      // Loads 32 score columns of this row, masking keys >= seq_len.
-      auto load_chunk = [&](int c, float *v) {
-        tmem_ld32(tS + c * 32, reinterpret_cast<uint32_t *>(v));
-        tmem_wait_ld();
-        reg_fence32(reinterpret_cast<uint32_t *>(v));
+      // Applies the key mask (keys >= seq_len -> -inf) to chunk c.
+      auto mask_chunk = [&](int c, float *v) {
         if (valid < C::BN) {
 #pragma unroll
           for (int i = 0; i < 32; i++)
             if (c * 32 + i >= valid) v[i] = -INFINITY;
         }
       };
-      // P = 2^(s*scale*log2e - m_used) as fp16 into the chunk's 16 columns.
-      auto emit_chunk = [&](int c, const float *v, float neg_m) {
-        uint32_t pk[16];
-        float sum = 0.0f;
+      // Pipelined pass over chunks [c_begin, 4) of this row: x = s*scale*
+      // log2e - m_used, P = 2^x as fp16 over the chunk's first 16 columns
+      // (chunk c's P lands in columns [16c, 16c+16), which belong to chunks
+      // already loaded), row sum of P accumulated into l_part. The TMEM load
+      // of chunk c+1 is in flight while chunk c is computed. With `check`,
+      // a chunk whose largest x exceeds 8 (P would pass 2^8) stops the pass
+      // before its P is stored; the return value is that chunk (4 = none).
+      auto emit_range = [&](auto cb, bool check, float &l_part) {
+        constexpr int c_begin = decltype(cb)::value;
+        uint32_t buf[2][32];
+        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        const float neg_m = -m_used;
+        int stop = 4;
 #pragma unroll
-        for (int i = 0; i < 16; i++) {
-          const float p0 = ex2_approx(fmaf(v[2 * i], sl2, neg_m));
-          const float p1 = ex2_approx(fmaf(v[2 * i + 1], sl2, neg_m));
-          sum += p0 + p1;
-          pk[i] = pack_f16x2(p0, p1);
+        for (int c = 0; c < 4; c++) {
+          if (c < c_begin || stop < 4) continue;
+          if (c == c_begin) tmem_ld32(tS + c * 32, buf[c & 1]);
+          tmem_wait_ld();
+          reg_fence32(buf[c & 1]);
+          if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
+          float *v = reinterpret_cast<float *>(buf[c & 1]);
+          mask_chunk(c, v);
+          float xm[8];
+#pragma unroll
+          for (int i = 0; i < 32; i++) {
+            v[i] = fmaf(v[i], sl2, neg_m);
+            xm[i & 7] = i < 8 ? v[i] : fmaxf(xm[i & 7], v[i]);
+          }
+          if (check) {
+            const float mc = fmaxf(fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])),
+                                   fmaxf(fmaxf(xm[4], xm[5]), fmaxf(xm[6], xm[7])));
+            if (__any_sync(0xffffffffu, mc > 8.0f)) {
+              stop = c;
+              continue;
+            }
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float p0 = ex2_approx(v[2 * i]), p1 = ex2_approx(v[2 * i + 1]);
+            part[i & 3] += p0 + p1;
+            pk[i] = pack_f16x2(p0, p1);
+          }
+          tmem_st16(tS + c * 16, pk);
         }
-        tmem_st16(tS + c * 16, pk);
-        return sum;
+        tmem_wait_ld();  // a prefetch may still be in flight after a stop
+        l_part += (part[0] + part[1]) + (part[2] + part[3]);
+        return stop;
+      };
+      // Largest raw score of chunks [c_begin, 4) (two loads in flight).
+      auto row_max = [&](auto cb) {
+        constexpr int c_begin = decltype(cb)::value;
+        uint32_t buf[2][32];
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          if (c < c_begin) continue;
+          if (c == c_begin) tmem_ld32(tS + c * 32, buf[c & 1]);
+          tmem_wait_ld();
+          reg_fence32(buf[c & 1]);
+          if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
+          float *v = reinterpret_cast<float *>(buf[c & 1]);
+          mask_chunk(c, v);
+#pragma unroll
+          for (int i = 0; i < 32; i++) mx[i & 3] = fmaxf(mx[i & 3], v[i]);
+        }
+        return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       };
       float l_blk = 0.0f;
-      // Fast path: the max used so far stays within 2^8 of every score of
-      // this block, so each chunk is exponentiated as soon as it is loaded.
-      bool restart = (j == 0);
-      if (!restart) {
-#pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-          float v[32];
-          load_chunk(c, v);
-          float mc = v[0];
-#pragma unroll
-          for (int i = 1; i < 32; i++) mc = fmaxf(mc, v[i]);
-          if (__any_sync(0xffffffffu, mc * sl2 > m_used + 8.0f)) {
-            restart = true;
-            break;
+      if (j == 0) {
+        // First block: no max yet. Row max, then P against it.
+        m_used = row_max(Chunk<0>{}) * sl2;
+        emit_range(Chunk<0>{}, false, l_blk);
+      } else {
+        // Exponentiate against the max used so far; a chunk with a score
+        // more than 2^8 above it stops the pass before its P is stored.
+        const int stop = emit_range(Chunk<0>{}, true, l_blk);
+        if (__any_sync(0xffffffffu, stop < 4)) {
+          // Rescale: chunks [0, stop) already hold P relative to the old max
+          // and their raw scores are partly overwritten; chunks [stop, 4)
+          // still hold raw scores. The new max comes from the latter (the
+          // former are within 2^8 of the old max by construction).
+          const int c0 = stop;  // warp-uniform: the vote stopped every lane
+          float mx_rest;
+          switch (c0) {
+            case 0: mx_rest = row_max(Chunk<0>{}); break;
+            case 1: mx_rest = row_max(Chunk<1>{}); break;
+            case 2: mx_rest = row_max(Chunk<2>{}); break;
+            default: mx_rest = row_max(Chunk<3>{}); break;
           }
-          l_blk += emit_chunk(c, v, -m_used);
-        }
-      }
-      if (restart) {
-        // Slow path: full row max first, then rescale O and l, then P.
-        float mx = -INFINITY;
-#pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-          float v[32];
-          load_chunk(c, v);
-#pragma unroll
-          for (int i = 0; i < 32; i++) mx = fmaxf(mx, v[i]);
-        }
-        const float m_new = mx * sl2;
-        const bool need = m_new > m_used + 8.0f;
-        const float m_tgt = need ? m_new : m_used;
-        const float factor = ex2_approx(m_used - m_tgt);  // 0 on the first block
-        l *= factor;
-        if (j > 0) {
+          const float m_new = fmaxf(mx_rest * sl2, m_used);
+          const float factor = ex2_approx(m_used - m_new);
+          l *= factor;
+          l_blk *= factor;
 #pragma unroll 1
           for (int c = 0; c < D / 32; c++) {
             uint32_t o[32];
@@ -347,14 +399,27 @@ __global__ void __launch_bounds__(320, 1)
             for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
             tmem_st32(tO + c * 32, o);
           }
-        }
-        m_used = m_tgt;
-        l_blk = 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-          float v[32];
-          load_chunk(c, v);
-          l_blk += emit_chunk(c, v, -m_used);
+#pragma unroll
+          for (int c = 0; c < 4; c++) {
+            if (c >= c0) continue;
+            uint32_t pk[16];
+            tmem_ld16(tS + c * 16, pk);
+            tmem_wait_ld();
+            reg_fence16(pk);
+#pragma unroll
+            for (int i = 0; i < 16; i++) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&pk[i]));
+              pk[i] = pack_f16x2(f.x * factor, f.y * factor);
+            }
+            tmem_st16(tS + c * 16, pk);
+          }
+          m_used = m_new;
+          switch (c0) {
+            case 0: emit_range(Chunk<0>{}, false, l_blk); break;
+            case 1: emit_range(Chunk<1>{}, false, l_blk); break;
+            case 2: emit_range(Chunk<2>{}, false, l_blk); break;
+            default: emit_range(Chunk<3>{}, false, l_blk); break;
+          }
         }
       }
       l += l_blk;

@@ -203,4 +203,27 @@ __global__ void merge_lse_kernel(float *la, const float *lb, long long n) {
   }
 }
 
+// dst[i] = OutT(src[i]) (RNE), 4 values per thread when aligned.
+template <typename OutT>
+__global__ void convert_f32_kernel(const float *src, OutT *dst, long long n, bool vec4) {
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (vec4) {
+    for (; 4 * i + 3 < n; i += stride) {
+      const float4 x = reinterpret_cast<const float4 *>(src)[i];
+      Pack<OutT, 4> o;
+      o.v[0] = from_f32<OutT>(x.x);
+      o.v[1] = from_f32<OutT>(x.y);
+      o.v[2] = from_f32<OutT>(x.z);
+      o.v[3] = from_f32<OutT>(x.w);
+      reinterpret_cast<Pack<OutT, 4> *>(dst)[i] = o;
+    }
+    // tail (n % 4 values) handled by thread 0 of block 0
+    if (blockIdx.x == 0 && threadIdx.x == 0)
+      for (long long t = n & ~3LL; t < n; t++) dst[t] = from_f32<OutT>(src[t]);
+  } else {
+    for (; i < n; i += stride) dst[i] = from_f32<OutT>(src[i]);
+  }
+}
+
 }  // namespace llmr

@@ -156,10 +156,7 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
   View<InT> vq{static_cast<const InT *>(q), qs[0], qs[1], qs[2]};
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
-  const long long rows = 3LL * pp.B * pp.S * pp.H;
-  long long blocks = (rows + 31) / 32;  // 8 warps x 4 rows per block
-  const long long cap = (long long)ctx->num_sms * 16;
-  if (blocks > cap) blocks = cap;
+  const dim3 blocks((pp.S + kProRowsPerCta - 1) / kProRowsPerCta, pp.B * pp.H, 3);
   // One vector access per lane needs every lane's first element aligned to
   // E elements: bases aligned and strides multiples of E; tables likewise.
   constexpr int E = D / 32;
@@ -172,9 +169,9 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
                    ok(v, vs, sizeof(InT) * E) && ok(pp.cos_t, nullptr, 4 * (E / 2)) &&
                    ok(pp.sin_t, nullptr, 4 * (E / 2));
   if (vec)
-    prologue_kernel<D, InT, OutT, true><<<(unsigned)blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
+    prologue_kernel<D, InT, OutT, true><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   else
-    prologue_kernel<D, InT, OutT, false><<<(unsigned)blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
+    prologue_kernel<D, InT, OutT, false><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   return after_launch(ctx, "prologue");
 }
 
@@ -499,6 +496,61 @@ int llmr_profile_read(llmr_ctx *ctx, float *ms2) {
   CUDA_TRY(ctx, cudaEventElapsedTime(&ms2[0], ctx->prof_ev[0], ctx->prof_ev[1]));
   CUDA_TRY(ctx, cudaEventElapsedTime(&ms2[1], ctx->prof_ev[1], ctx->prof_ev[2]));
   return LLMR_OK;
+}
+
+int llmr_attention_prologue(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
+                            const void *k, const void *v, const float *q_gain,
+                            const float *k_gain, const float *cos_t, const float *sin_t,
+                            void *qkv_out) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!d || !q || !k || !v || !qkv_out) return fail(ctx, LLMR_EINVAL, "null argument");
+  const int B = d->batch, H = d->n_heads, S = d->seq_len, D = d->head_dim;
+  if (B < 1 || H < 1 || S < 1) return fail(ctx, LLMR_EINVAL, "batch, n_heads, seq_len must be >= 1");
+  if (D != 64 && D != 128) return fail(ctx, LLMR_EINVAL, "head_dim %d unsupported (64 or 128)", D);
+  if ((long long)B * H > 65535) return fail(ctx, LLMR_EINVAL, "batch*n_heads exceeds 65535");
+  if (d->in_dtype > LLMR_BF16 || d->layout > LLMR_LAYOUT_BHSD)
+    return fail(ctx, LLMR_EINVAL, "bad dtype or layout");
+  if (d->flags & LLMR_EXACT) return fail(ctx, LLMR_EINVAL, "the prologue writes fp16 operands");
+  if ((d->flags & LLMR_NORM_Q) && !q_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_Q needs q_gain");
+  if ((d->flags & LLMR_NORM_K) && !k_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_K needs k_gain");
+  if ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) return fail(ctx, LLMR_EINVAL, "LLMR_ROPE needs cos/sin tables");
+  if (reinterpret_cast<uintptr_t>(qkv_out) & 15)
+    return fail(ctx, LLMR_EINVAL, "qkv_out must be 16-byte aligned");
+  long long qs[3], ks[3], vs[3];
+  default_strides(d, d->q_row_stride, d->q_batch_stride, d->q_head_stride, qs);
+  default_strides(d, d->k_row_stride, d->k_batch_stride, d->k_head_stride, ks);
+  default_strides(d, d->v_row_stride, d->v_batch_stride, d->v_head_stride, vs);
+  ProParams pp;
+  pp.B = B;
+  pp.S = S;
+  pp.H = H;
+  pp.split_row = (int)d->split_row;
+  pp.rope_row_offset = (int)d->rope_row_offset;
+  pp.eps = d->eps;
+  pp.q_gain = (d->flags & LLMR_NORM_Q) ? q_gain : nullptr;
+  pp.k_gain = (d->flags & LLMR_NORM_K) ? k_gain : nullptr;
+  pp.cos_t = (d->flags & LLMR_ROPE) ? cos_t : nullptr;
+  pp.sin_t = (d->flags & LLMR_ROPE) ? sin_t : nullptr;
+  return launch_prologue<__half>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs,
+                                 static_cast<__half *>(qkv_out), pp);
+}
+
+int llmr_convert_f32(llmr_ctx *ctx, const float *src, void *dst, llmr_dtype dt, size_t n) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!src || !dst || dt > LLMR_BF16) return fail(ctx, LLMR_EINVAL, "bad argument");
+  if (n == 0) return LLMR_OK;
+  const bool vec4 = (reinterpret_cast<uintptr_t>(src) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(dst) & (dt == LLMR_F32 ? 15 : 7)) == 0;
+  const unsigned grid = grid_for(ctx, (long long)(vec4 ? (n + 3) / 4 : n), 256);
+  if (dt == LLMR_F32)
+    convert_f32_kernel<float><<<grid, 256, 0, ctx->stream>>>(src, static_cast<float *>(dst), (long long)n, vec4);
+  else if (dt == LLMR_F16)
+    convert_f32_kernel<__half><<<grid, 256, 0, ctx->stream>>>(src, static_cast<__half *>(dst), (long long)n, vec4);
+  else
+    convert_f32_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(src, static_cast<__nv_bfloat16 *>(dst), (long long)n, vec4);
+  return after_launch(ctx, "convert_f32");
 }
 
 int llmr_flash_attention_v2(llmr_ctx *ctx, const float *q, const float *k, const float *v,

@@ -128,9 +128,8 @@ int prologue(cudaStream_t st, int num_sms, const void *q, const void *k, const v
   View<InT> vq{static_cast<const InT *>(q), qs[0], qs[1], qs[2]};
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
-  const long long rows = 3LL * pp.B * pp.S * pp.H;
-  long long blocks = (rows + 31) / 32;
-  if (blocks > (long long)num_sms * 16) blocks = (long long)num_sms * 16;
+  (void)num_sms;
+  const dim3 blocks((pp.S + kProRowsPerCta - 1) / kProRowsPerCta, pp.B * pp.H, 3);
   auto ok = [&](const void *ptr, const long long *s, size_t bytes) {
     return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) % bytes) == 0 &&
                               (s == nullptr || (s[0] % E == 0 && s[1] % E == 0 && s[2] % E == 0)));
@@ -139,9 +138,9 @@ int prologue(cudaStream_t st, int num_sms, const void *q, const void *k, const v
                    ok(v, vs, sizeof(InT) * E) && ok(pp.cos_t, nullptr, 4 * (E / 2)) &&
                    ok(pp.sin_t, nullptr, 4 * (E / 2));
   if (vec)
-    prologue_kernel<D, InT, __half, true><<<(unsigned)blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
+    prologue_kernel<D, InT, __half, true><<<blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
   else
-    prologue_kernel<D, InT, __half, false><<<(unsigned)blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
+    prologue_kernel<D, InT, __half, false><<<blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
   return cudaGetLastError() == cudaSuccess ? LLMR_OK : LLMR_ECUDA;
 }
 

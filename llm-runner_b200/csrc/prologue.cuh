@@ -39,9 +39,15 @@ struct alignas(sizeof(T) * N) Pack {
   T v[N];
 };
 
-// One warp per (tensor, b, s, h) row of D elements, 4 rows in flight per
-// warp. Q and K rows get the per-head RMSNorm of batch_head_norm
-// (dependencies/zimage.c3l/shaders/zimage.slang:623-659:
+// Rows per CTA of the prologue: 8 warps x 4 rows in flight per warp.
+constexpr int kProRowsPerWarp = 4;
+constexpr int kProWarps = 8;
+constexpr int kProRowsPerCta = kProRowsPerWarp * kProWarps;
+
+// Grid (ceil(S / 32), B*H, 3): blockIdx.z selects Q, K or V, blockIdx.y the
+// (b, h) unit, and each warp owns 4 consecutive tokens s of that unit (a
+// row = D elements). Q and K rows get the per-head RMSNorm of
+// batch_head_norm (dependencies/zimage.c3l/shaders/zimage.slang:623-659:
 // x * (1/sqrt(mean(x^2) + eps)) * g) and the interleaved rotation of mrope
 // (dependencies/zimage.c3l/shaders/mrope.slang:47-53), computed in fp32 with
 // the same operation order; V is only converted. Output: dense
@@ -53,90 +59,80 @@ __global__ void __launch_bounds__(256)
     prologue_kernel(View<InT> q, View<InT> k, View<InT> v, OutT *out,
                     ProParams p) {
   constexpr int E = D / 32;  // elements per lane: 4 (D=128) or 2 (D=64)
-  constexpr int U = 4;       // rows per warp per iteration
+  constexpr int U = kProRowsPerWarp;
   const int lane = threadIdx.x & 31;
-  const long long rows = (long long)p.B * p.S * p.H;
-  const long long total = 3 * rows;
-  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
-  const long long plane = rows * D;
-  for (long long w0 = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       w0 < total; w0 += U * warps) {
-    float x[U][E];
-    int tsel[U], s[U];
-    long long r[U];
+  const int t = blockIdx.z;  // 0 = Q, 1 = K, 2 = V
+  const int bh = blockIdx.y;
+  const int b = bh / p.H, h = bh - b * p.H;
+  const int s0 = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * U;
+  // Select by value (a reference into the parameter block would force it
+  // into local memory).
+  const InT *base = t == 0 ? q.base : (t == 1 ? k.base : v.base);
+  const long long bs = t == 0 ? q.bs : (t == 1 ? k.bs : v.bs);
+  const long long rs = t == 0 ? q.rs : (t == 1 ? k.rs : v.rs);
+  const long long hs = t == 0 ? q.hs : (t == 1 ? k.hs : v.hs);
+  const InT *src0 = base + (long long)b * bs + (long long)h * hs + lane * E;
+  float x[U][E];
 #pragma unroll
-    for (int u = 0; u < U; u++) {
-      const long long w = w0 + u * warps;
-      tsel[u] = w < total ? (int)(w / rows) : 0;
-      r[u] = w - tsel[u] * rows;
-      s[u] = (int)(r[u] % p.S);
-      if (w >= total) continue;
-      // r enumerates (b, h, s) with s fastest, matching the output order.
-      const long long bh = r[u] / p.S;
-      const int h = (int)(bh % p.H), b = (int)(bh / p.H);
-      // Select by value (a reference into the parameter block would force it
-      // into local memory).
-      const int t = tsel[u];
-      const InT *base = t == 0 ? q.base : (t == 1 ? k.base : v.base);
-      const long long bs = t == 0 ? q.bs : (t == 1 ? k.bs : v.bs);
-      const long long rs = t == 0 ? q.rs : (t == 1 ? k.rs : v.rs);
-      const long long hs = t == 0 ? q.hs : (t == 1 ? k.hs : v.hs);
-      const InT *src = base + b * bs + (long long)s[u] * rs + (long long)h * hs + lane * E;
+  for (int u = 0; u < U; u++) {
+    if (s0 + u >= p.S) break;
+    const InT *src = src0 + (long long)(s0 + u) * rs;
+    if (VEC) {
+      const Pack<InT, E> pk = *reinterpret_cast<const Pack<InT, E> *>(src);
+#pragma unroll
+      for (int e = 0; e < E; e++) x[u][e] = to_f32<InT>(pk.v[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; e++) x[u][e] = to_f32<InT>(src[e]);
+    }
+  }
+  const float *gain = t == 0 ? p.q_gain : (t == 1 ? p.k_gain : nullptr);
+  OutT *dst0 = out + ((long long)t * p.B * p.H + bh) * (long long)p.S * D + lane * E;
+#pragma unroll
+  for (int u = 0; u < U; u++) {
+    const int s = s0 + u;
+    if (s >= p.S) break;
+    const long long grow = (long long)p.rope_row_offset + s;  // global token index
+    if (gain != nullptr) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int e = 0; e < E; e++) ss = __fmaf_rn(x[u][e], x[u][e], ss);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rms = 1.0f / sqrtf(ss / (float)D + p.eps);
+      const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + lane * E;
+#pragma unroll
+      for (int e = 0; e < E; e++) x[u][e] = __fmul_rn(__fmul_rn(x[u][e], rms), g[e]);
+    }
+    if (t < 2 && p.cos_t != nullptr) {
+      const long long trow = grow * (D / 2) + lane * (E / 2);
+      float cv[E / 2], sv[E / 2];
       if (VEC) {
-        const Pack<InT, E> pk = *reinterpret_cast<const Pack<InT, E> *>(src);
+        const Pack<float, E / 2> pc = *reinterpret_cast<const Pack<float, E / 2> *>(p.cos_t + trow);
+        const Pack<float, E / 2> ps = *reinterpret_cast<const Pack<float, E / 2> *>(p.sin_t + trow);
 #pragma unroll
-        for (int e = 0; e < E; e++) x[u][e] = to_f32<InT>(pk.v[e]);
+        for (int e = 0; e < E / 2; e++) {
+          cv[e] = pc.v[e];
+          sv[e] = ps.v[e];
+        }
       } else {
 #pragma unroll
-        for (int e = 0; e < E; e++) x[u][e] = to_f32<InT>(src[e]);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; u++) {
-      if (w0 + u * warps >= total) break;
-      const float *gain = tsel[u] == 0 ? p.q_gain : (tsel[u] == 1 ? p.k_gain : nullptr);
-      const long long grow = (long long)p.rope_row_offset + s[u];  // global token index
-      if (gain != nullptr) {
-        float ss = 0.0f;
-#pragma unroll
-        for (int e = 0; e < E; e++) ss = __fmaf_rn(x[u][e], x[u][e], ss);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-        const float rms = 1.0f / sqrtf(ss / (float)D + p.eps);
-        const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + lane * E;
-#pragma unroll
-        for (int e = 0; e < E; e++) x[u][e] = __fmul_rn(__fmul_rn(x[u][e], rms), g[e]);
-      }
-      if (tsel[u] < 2 && p.cos_t != nullptr) {
-        const long long trow = grow * (D / 2) + lane * (E / 2);
-        float cv[E / 2], sv[E / 2];
-        if (VEC) {
-          const Pack<float, E / 2> pc = *reinterpret_cast<const Pack<float, E / 2> *>(p.cos_t + trow);
-          const Pack<float, E / 2> ps = *reinterpret_cast<const Pack<float, E / 2> *>(p.sin_t + trow);
-#pragma unroll
-          for (int e = 0; e < E / 2; e++) {
-            cv[e] = pc.v[e];
-            sv[e] = ps.v[e];
-          }
-        } else {
-#pragma unroll
-          for (int e = 0; e < E / 2; e++) {
-            cv[e] = p.cos_t[trow + e];
-            sv[e] = p.sin_t[trow + e];
-          }
-        }
-#pragma unroll
-        for (int e = 0; e < E; e += 2) {
-          const float x0 = x[u][e], x1 = x[u][e + 1];
-          x[u][e] = __fsub_rn(__fmul_rn(x0, cv[e / 2]), __fmul_rn(x1, sv[e / 2]));
-          x[u][e + 1] = __fadd_rn(__fmul_rn(x0, sv[e / 2]), __fmul_rn(x1, cv[e / 2]));
+        for (int e = 0; e < E / 2; e++) {
+          cv[e] = p.cos_t[trow + e];
+          sv[e] = p.sin_t[trow + e];
         }
       }
-      Pack<OutT, E> po;
 #pragma unroll
-      for (int e = 0; e < E; e++) po.v[e] = from_f32<OutT>(x[u][e]);
-      *reinterpret_cast<Pack<OutT, E> *>(out + tsel[u] * plane + r[u] * D + lane * E) = po;
+      for (int e = 0; e < E; e += 2) {
+        const float x0 = x[u][e], x1 = x[u][e + 1];
+        x[u][e] = __fsub_rn(__fmul_rn(x0, cv[e / 2]), __fmul_rn(x1, sv[e / 2]));
+        x[u][e + 1] = __fadd_rn(__fmul_rn(x0, sv[e / 2]), __fmul_rn(x1, cv[e / 2]));
+      }
     }
+    Pack<OutT, E> po;
+#pragma unroll
+    for (int e = 0; e < E; e++) po.v[e] = from_f32<OutT>(x[u][e]);
+    *reinterpret_cast<Pack<OutT, E> *>(dst0 + (long long)s * D) = po;
   }
 }
 

@@ -103,6 +103,9 @@ def _load() -> ctypes.CDLL:
         "llmr_attention_fused": (i32, [vp, ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp]),
         "llmr_attention_merge": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, u64]),
+        "llmr_attention_prologue": (i32, [vp, ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
+                                          vp, vp, vp]),
+        "llmr_convert_f32": (i32, [vp, vp, vp, ctypes.c_int, ctypes.c_size_t]),
         "llmr_attention_fused_noalloc": (i32, [ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                                vp, vp, vp, vp, vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
@@ -327,6 +330,22 @@ def attention_fused_noalloc(q, k, v, o, cfg: AttnConfig, *, batch: int, seq_len:
                                           _ptr(o), _ptr(lse), ctypes.c_void_p(raw or None))
     if rc != OK:
         raise LlmrError(rc, "llmr_attention_fused_noalloc")
+
+
+def attention_prologue(ctx: Context, q, k, v, qkv_out, cfg: AttnConfig, *, batch: int,
+                       seq_len: int, q_gain=None, k_gain=None, cos=None, sin=None,
+                       strides: Optional[dict] = None) -> None:
+    """Norm + RoPE of Q/K and cast of V into dense fp16 [3][B][H][S][D]."""
+    desc = make_desc(cfg, batch, seq_len, _dtype_code(q), F16, strides=strides)
+    ctx.check(lib.llmr_attention_prologue(ctx.handle, ctypes.byref(desc), _ptr(q), _ptr(k),
+                                          _ptr(v), _ptr(q_gain), _ptr(k_gain), _ptr(cos),
+                                          _ptr(sin), _ptr(qkv_out)))
+
+
+def convert_f32(ctx: Context, src, dst) -> None:
+    """dst <- src (fp32) converted to dst's dtype with RNE."""
+    ctx.check(lib.llmr_convert_f32(ctx.handle, _ptr(src), _ptr(dst), _dtype_code(dst),
+                                   src.numel()))
 
 
 def attention_merge(ctx: Context, o_a, lse_a, o_b, lse_b, rows: int, n_heads: int,

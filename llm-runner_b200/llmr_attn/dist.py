@@ -1,0 +1,160 @@
+"""Multi-GPU execution of the attention path (one process per GPU).
+
+Two schemes, both new relative to the reference (which is single-GPU,
+`docs/flux_server.md:84-88`):
+
+* (batch x head) partition, no collective. The B*H (b, h) units are
+  independent, so rank r of N computes the contiguous unit range
+  [r*U/N, (r+1)*U/N) straight from strided views of the full tensors and
+  writes its slice of O. `partition_units` / `head_split_attention`.
+
+* Sequence-sharded ring for long sequences. Rank r holds tokens
+  [r*S/P, (r+1)*S/P). It normalises and rotates its own Q/K once (global
+  RoPE rows and global txt/img gain split), then runs P steps: attention of
+  its Q against the K/V block it currently holds (fp32 partial O + LSE),
+  merged into the running result by log-sum-exp, while the block is passed
+  to rank r+1 and the next one received from rank r-1 by NCCL P2P
+  (batch_isend_irecv) on NCCL's stream, overlapping the attention kernel.
+  `RingAttention`.
+
+The ring's schedule and merge are plain host logic over pluggable ops, so
+they are exercised on CPU with gloo ranks as well as on GPUs with NCCL.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Tuple
+
+import llmr_attn as L
+
+
+# ---------------------------------------------------------------- head split
+
+def partition_units(batch: int, n_heads: int, world: int, rank: int) -> List[Tuple[int, int, int]]:
+    """Rank `rank`'s share of the batch*n_heads (b, h) units as runs
+    (b, h0, h1) inside single batch elements. Shares differ by at most one
+    unit (Z-Image's 60 units on 8 GPUs: four ranks get 8, four get 7)."""
+    if world < 1 or not 0 <= rank < world:
+        raise ValueError("bad rank/world")
+    units = batch * n_heads
+    lo = rank * units // world
+    hi = (rank + 1) * units // world
+    runs = []
+    u = lo
+    while u < hi:
+        b, h0 = divmod(u, n_heads)
+        h1 = min(n_heads, h0 + (hi - u))
+        runs.append((b, h0, h1))
+        u += h1 - h0
+    return runs
+
+
+def head_split_attention(ctx: "L.Context", q, k, v, o, cfg: "L.AttnConfig", *, batch: int,
+                         seq_len: int, rank: int, world: int, q_gain=None, k_gain=None,
+                         cos=None, sin=None) -> List[Tuple[int, int, int]]:
+    """This rank's (b, h) units of the fused op. q/k/v are the full BSHD
+    [B,S,H,D] tensors (or views of them), o the full [B,S,H*D] output; only
+    this rank's head slices of o are written. No communication."""
+    H, D = cfg.n_heads, cfg.head_dim
+    if cfg.layout != L.BSHD:
+        raise ValueError("head_split_attention expects BSHD inputs")
+    runs = partition_units(batch, H, world, rank)
+    for b, h0, h1 in runs:
+        sub = L.AttnConfig(**{**cfg.__dict__, "n_heads": h1 - h0})
+        st = {"q_row_stride": q.stride(1), "k_row_stride": k.stride(1),
+              "v_row_stride": v.stride(1), "q_head_stride": q.stride(2),
+              "k_head_stride": k.stride(2), "v_head_stride": v.stride(2),
+              "o_row_stride": o.stride(1)}
+        L.attention_fused(ctx, q[b, :, h0:h1], k[b, :, h0:h1], v[b, :, h0:h1],
+                          o[b, :, h0 * D:h1 * D], sub, batch=1, seq_len=seq_len,
+                          q_gain=q_gain, k_gain=k_gain, cos=cos, sin=sin, strides=st)
+    return runs
+
+
+# ---------------------------------------------------------------------- ring
+
+class RingOps:
+    """The four device steps of the ring, on the library's CUDA kernels."""
+
+    def __init__(self, ctx: "L.Context", cfg: "L.AttnConfig", seq_local: int,
+                 row_offset: int):
+        self.ctx, self.cfg, self.S, self.off = ctx, cfg, seq_local, row_offset
+        self.part_cfg = L.AttnConfig(n_heads=cfg.n_heads, head_dim=cfg.head_dim,
+                                     scale=cfg.scale, layout=L.BHSD)
+
+    def empty(self, shape, dtype, device):
+        import torch
+        return torch.empty(shape, dtype=dtype, device=device)
+
+    def prologue(self, q, k, v, qkv_out, q_gain, k_gain, cos, sin):
+        pc = L.AttnConfig(**{**self.cfg.__dict__, "rope_row_offset": self.off})
+        L.attention_prologue(self.ctx, q, k, v, qkv_out, pc, batch=1, seq_len=self.S,
+                             q_gain=q_gain, k_gain=k_gain, cos=cos, sin=sin)
+
+    def partial(self, qh, kh, vh, o, lse):
+        L.attention_fused(self.ctx, qh, kh, vh, o, self.part_cfg, batch=1, seq_len=self.S,
+                          lse=lse)
+
+    def merge(self, o_acc, lse_acc, o_t, lse_t):
+        L.attention_merge(self.ctx, o_acc, lse_acc, o_t, lse_t, self.S, self.cfg.n_heads,
+                          self.cfg.head_dim)
+
+    def finalize(self, o_acc, out):
+        L.convert_f32(self.ctx, o_acc, out)
+
+
+@dataclass
+class RingBuffers:
+    qkv: object      # fp16 [3, H, S_loc, D] (Q', K', V' of this rank)
+    kv_nxt: object   # fp16 [2, H, S_loc, D] (receive buffer)
+    o_acc: object    # fp32 [S_loc, H*D]
+    lse_acc: object  # fp32 [H, S_loc]
+    o_tmp: object
+    lse_tmp: object
+
+
+class RingAttention:
+    """Sequence-sharded ring attention over a torch.distributed group."""
+
+    def __init__(self, ops, n_heads: int, head_dim: int, seq_total: int, rank: int,
+                 world: int, device, group=None, qkv_dtype=None):
+        import torch
+        if seq_total % world:
+            raise ValueError("seq_total must divide evenly over the ring")
+        self.ops, self.rank, self.world, self.group = ops, rank, world, group
+        self.S = seq_total // world
+        H, D, S = n_heads, head_dim, self.S
+        dt = qkv_dtype or torch.float16
+        self.buf = RingBuffers(
+            qkv=ops.empty((3, H, S, D), dt, device),
+            kv_nxt=ops.empty((2, H, S, D), dt, device),
+            o_acc=ops.empty((S, H * D), torch.float32, device),
+            lse_acc=ops.empty((H, S), torch.float32, device),
+            o_tmp=ops.empty((S, H * D), torch.float32, device),
+            lse_tmp=ops.empty((H, S), torch.float32, device))
+
+    def forward(self, q, k, v, out, q_gain=None, k_gain=None, cos=None, sin=None) -> None:
+        """q/k/v: this rank's token shard [1, S_loc, H, D]; out: [1, S_loc, H*D]."""
+        import torch.distributed as dist
+        b = self.buf
+        self.ops.prologue(q, k, v, b.qkv, q_gain, k_gain, cos, sin)
+        qh = b.qkv[0]
+        kv_cur, kv_nxt = b.qkv[1:3], b.kv_nxt
+        nxt_rank = (self.rank + 1) % self.world
+        prv_rank = (self.rank - 1) % self.world
+        for t in range(self.world):
+            reqs = None
+            if t < self.world - 1:
+                reqs = dist.batch_isend_irecv([
+                    dist.P2POp(dist.isend, kv_cur, nxt_rank, self.group),
+                    dist.P2POp(dist.irecv, kv_nxt, prv_rank, self.group)])
+            if t == 0:
+                self.ops.partial(qh, kv_cur[0], kv_cur[1], b.o_acc, b.lse_acc)
+            else:
+                self.ops.partial(qh, kv_cur[0], kv_cur[1], b.o_tmp, b.lse_tmp)
+                self.ops.merge(b.o_acc, b.lse_acc, b.o_tmp, b.lse_tmp)
+            if reqs is not None:
+                for w in reqs:
+                    w.wait()
+            kv_cur, kv_nxt = kv_nxt, kv_cur
+        self.ops.finalize(b.o_acc, out)

@@ -157,6 +157,34 @@ def test_tc_kernel_ragged_shapes(ctx, D, S):
     check(host(o), oracle_fa(q, k, v, scale).reshape(B, S, H * D), what=f"S={S} D={D}")
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_tc_kernel_rescale_paths(ctx, D):
+    """Scores that jump by more than 2^8 (in P) inside later key blocks, at
+    every 32-key chunk position, force the lazy-rescale path: O and the P
+    already written for earlier chunks are rescaled in place."""
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(21 + D)
+    B, S, H = 1, 900, 2
+    q = rng.standard_normal((B, S, H, D), dtype=np.float32) * 0.2
+    k = rng.standard_normal((B, S, H, D), dtype=np.float32) * 0.2
+    v = rng.standard_normal((B, S, H, D), dtype=np.float32)
+    q[..., 0] += 2.0                     # every query shares a component on dim 0
+    # (key position, size): block 1 chunk 0, block 2 chunk 1, block 3 chunk 3,
+    # block 4 chunk 2, block 6 chunk 0 -- each jump is well over 8 in log2(P).
+    for pos, size in ((150, 10.0), (2 * 128 + 40, 60.0), (3 * 128 + 100, 150.0),
+                      (4 * 128 + 70, 300.0), (6 * 128 + 5, 600.0)):
+        k[0, pos, :, :] = 0.0
+        k[0, pos, :, 0] = size
+    q, k, v = (a.astype(np.float16).astype(np.float32) for a in (q, k, v))
+    scale = D ** -0.5
+    o = torch.empty((B, S, H * D), device="cuda", dtype=torch.float32)
+    L.attention_fused(ctx, dev(q).half(), dev(k).half(), dev(v).half(), o,
+                      L.AttnConfig(n_heads=H, head_dim=D, scale=scale), batch=B, seq_len=S)
+    ctx.sync()
+    check(host(o), oracle_fa(q, k, v, scale).reshape(B, S, H * D), what=f"rescale D={D}")
+
+
 @pytest.mark.parametrize("in_dt", ["f32", "f16", "bf16"])
 @pytest.mark.parametrize("out_dt", ["f32", "f16", "bf16"])
 def test_tc_kernel_dtypes(ctx, in_dt, out_dt):
