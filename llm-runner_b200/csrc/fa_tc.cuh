@@ -18,7 +18,7 @@
 // other tile's GEMMs):
 //   PV0_j, S0_{j+1}, PV1_j, S1_{j+1}
 // The softmax rescales O lazily: only when a row max grows by more than
-// 2^8 over the max used so far (so fp16 P stays <= 256).
+// 2^15 over the max used so far (so fp16 P stays <= 32768).
 #pragma once
 #include "ptx.cuh"
 
@@ -60,16 +60,21 @@ __device__ __forceinline__ void reg_fence32(uint32_t *r) {
 #pragma unroll
   for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
 }
-__device__ __forceinline__ void reg_fence16(uint32_t *r) {
-#pragma unroll
-  for (int i = 0; i < 16; i++) asm volatile("" : "+r"(r[i]));
-}
 
-// Compile-time chunk index for the softmax's chunk loops.
-template <int N>
-struct Chunk {
-  static constexpr int value = N;
-};
+// Which of the 16 exponential pairs of a 32-column chunk are computed on the
+// FMA pipe (exp2_poly_x2) instead of MUFU ex2: bit i set = pair i. Sharing
+// the work between the two pipes keeps MUFU (which also packs P to fp16) from
+// bounding the softmax.
+#ifndef LLMR_EXP2_EMU_MASK
+#define LLMR_EXP2_EMU_MASK 0x1111u  // 1 pair in 4: the measured optimum on B200
+#endif
+constexpr uint32_t kExp2EmuMask = LLMR_EXP2_EMU_MASK;
+
+// Largest exponent argument x = s*scale*log2e - m the softmax lets through
+// without rescaling: P = 2^x <= 2^15 stays finite in fp16 (max 65504) with
+// the same 2^-11 relative rounding as any other value, and O / l accumulate
+// in fp32. A row max growing past this triggers the (rare) rescale path.
+constexpr float kMaxExp = 15.0f;
 
 template <typename OutT>
 __device__ __forceinline__ void store_row_chunk(OutT *dst, const float *v);
@@ -295,100 +300,71 @@ __global__ void __launch_bounds__(320, 1)
             if (c * 32 + i >= valid) v[i] = -INFINITY;
         }
       };
-      // Pipelined pass over chunks [c_begin, 4) of this row: x = s*scale*
-      // log2e - m_used, P = 2^x as fp16 over the chunk's first 16 columns
-      // (chunk c's P lands in columns [16c, 16c+16), which belong to chunks
-      // already loaded), row sum of P accumulated into l_part. The TMEM load
-      // of chunk c+1 is in flight while chunk c is computed. With `check`,
-      // a chunk whose largest x exceeds 8 (P would pass 2^8) stops the pass
-      // before its P is stored; the return value is that chunk (4 = none).
-      auto emit_range = [&](auto cb, bool check, float &l_part) {
-        constexpr int c_begin = decltype(cb)::value;
+      // Pass 1: the row max of this block's raw scores, streaming the four
+      // 32-column chunks with the next chunk's TMEM load in flight.
+      auto row_max = [&]() {
         uint32_t buf[2][32];
-        float part[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        const float neg_m = -m_used;
-        int stop = 4;
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        tmem_ld32(tS, buf[0]);
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          if (c < c_begin || stop < 4) continue;
-          if (c == c_begin) tmem_ld32(tS + c * 32, buf[c & 1]);
           tmem_wait_ld();
           reg_fence32(buf[c & 1]);
           if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
           float *v = reinterpret_cast<float *>(buf[c & 1]);
           mask_chunk(c, v);
-          float xm[8];
 #pragma unroll
-          for (int i = 0; i < 32; i++) {
-            v[i] = fmaf(v[i], sl2, neg_m);
-            xm[i & 7] = i < 8 ? v[i] : fmaxf(xm[i & 7], v[i]);
-          }
-          if (check) {
-            const float mc = fmaxf(fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3])),
-                                   fmaxf(fmaxf(xm[4], xm[5]), fmaxf(xm[6], xm[7])));
-            if (__any_sync(0xffffffffu, mc > 8.0f)) {
-              stop = c;
-              continue;
-            }
-          }
+          for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = max3f(mx[(i >> 1) & 3], v[i], v[i + 1]);
+        }
+        return max3f(mx[0], mx[1], fmaxf(mx[2], mx[3]));
+      };
+      // Pass 2: P = 2^(s*scale*log2e - m_used) as fp16 over each chunk's
+      // first 16 columns (chunk c's P lands in columns [16c, 16c+16), which
+      // belong to chunks already loaded); returns the row sum of P. No
+      // branches: every chunk is loaded (next one in flight), scaled with a
+      // packed FMA, exponentiated (a share of the pairs on the FMA pipe) and
+      // stored.
+      auto emit_all = [&]() {
+        uint32_t buf[2][32];
+        uint64_t part2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
+        const uint64_t neg_mx2 = f2_pack(-m_used, -m_used);
+        tmem_ld32(tS, buf[0]);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          tmem_wait_ld();
+          reg_fence32(buf[c & 1]);
+          if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
+          float *v = reinterpret_cast<float *>(buf[c & 1]);
+          mask_chunk(c, v);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; i++) {
-            const float p0 = ex2_approx(v[2 * i]), p1 = ex2_approx(v[2 * i + 1]);
-            part[i & 3] += p0 + p1;
-            pk[i] = pack_f16x2(p0, p1);
+            const float2 x = f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), sl2x2, neg_mx2));
+            uint64_t pp;
+            if ((kExp2EmuMask >> i) & 1u)  // this pair's exponentials on the FMA pipe
+              pp = exp2_poly_x2(f2_pack(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f)));
+            else
+              pp = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
+            part2[i & 1] = f2_add(part2[i & 1], pp);
+            const float2 pf = f2_unpack(pp);
+            pk[i] = pack_f16x2(pf.x, pf.y);
           }
           tmem_st16(tS + c * 16, pk);
         }
-        tmem_wait_ld();  // a prefetch may still be in flight after a stop
-        l_part += (part[0] + part[1]) + (part[2] + part[3]);
-        return stop;
+        const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
+        return (s0.x + s0.y) + (s1.x + s1.y);
       };
-      // Largest raw score of chunks [c_begin, 4) (two loads in flight).
-      auto row_max = [&](auto cb) {
-        constexpr int c_begin = decltype(cb)::value;
-        uint32_t buf[2][32];
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < 4; c++) {
-          if (c < c_begin) continue;
-          if (c == c_begin) tmem_ld32(tS + c * 32, buf[c & 1]);
-          tmem_wait_ld();
-          reg_fence32(buf[c & 1]);
-          if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
-          float *v = reinterpret_cast<float *>(buf[c & 1]);
-          mask_chunk(c, v);
-#pragma unroll
-          for (int i = 0; i < 32; i++) mx[i & 3] = fmaxf(mx[i & 3], v[i]);
-        }
-        return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      };
-      float l_blk = 0.0f;
-      if (j == 0) {
-        // First block: no max yet. Row max, then P against it.
-        m_used = row_max(Chunk<0>{}) * sl2;
-        emit_range(Chunk<0>{}, false, l_blk);
-      } else {
-        // Exponentiate against the max used so far; a chunk with a score
-        // more than 2^8 above it stops the pass before its P is stored.
-        const int stop = emit_range(Chunk<0>{}, true, l_blk);
-        if (__any_sync(0xffffffffu, stop < 4)) {
-          // Rescale: chunks [0, stop) already hold P relative to the old max
-          // and their raw scores are partly overwritten; chunks [stop, 4)
-          // still hold raw scores. The new max comes from the latter (the
-          // former are within 2^8 of the old max by construction).
-          const int c0 = stop;  // warp-uniform: the vote stopped every lane
-          float mx_rest;
-          switch (c0) {
-            case 0: mx_rest = row_max(Chunk<0>{}); break;
-            case 1: mx_rest = row_max(Chunk<1>{}); break;
-            case 2: mx_rest = row_max(Chunk<2>{}); break;
-            default: mx_rest = row_max(Chunk<3>{}); break;
-          }
-          const float m_new = fmaxf(mx_rest * sl2, m_used);
-          const float factor = ex2_approx(m_used - m_new);
-          l *= factor;
-          l_blk *= factor;
+      // Lazy max: the max the P values are relative to moves only when this
+      // block's row max passes it by more than kMaxExp (P would overflow
+      // fp16), and on the first block; O and l are rescaled then.
+      const float m_new = row_max() * sl2;
+      const bool need = m_new > m_used + kMaxExp;  // always true on block 0
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_tgt = need ? m_new : m_used;
+        const float factor = ex2_approx(m_used - m_tgt);  // 0 on the first block
+        l *= factor;
+        if (j > 0) {
 #pragma unroll 1
           for (int c = 0; c < D / 32; c++) {
             uint32_t o[32];
@@ -399,29 +375,10 @@ __global__ void __launch_bounds__(320, 1)
             for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
             tmem_st32(tO + c * 32, o);
           }
-#pragma unroll
-          for (int c = 0; c < 4; c++) {
-            if (c >= c0) continue;
-            uint32_t pk[16];
-            tmem_ld16(tS + c * 16, pk);
-            tmem_wait_ld();
-            reg_fence16(pk);
-#pragma unroll
-            for (int i = 0; i < 16; i++) {
-              const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&pk[i]));
-              pk[i] = pack_f16x2(f.x * factor, f.y * factor);
-            }
-            tmem_st16(tS + c * 16, pk);
-          }
-          m_used = m_new;
-          switch (c0) {
-            case 0: emit_range(Chunk<0>{}, false, l_blk); break;
-            case 1: emit_range(Chunk<1>{}, false, l_blk); break;
-            case 2: emit_range(Chunk<2>{}, false, l_blk); break;
-            default: emit_range(Chunk<3>{}, false, l_blk); break;
-          }
         }
+        m_used = m_tgt;
       }
+      const float l_blk = emit_all();
       l += l_blk;
       tmem_wait_st();
       tc_fence_before();

@@ -200,19 +200,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t *r) {
       : "memory");
 }
 
-// 16 consecutive 32-bit TMEM columns of this thread's lane -> r[0..15].
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t *r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]),
-        "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]),
-        "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
-        "=r"(r[15])
-      : "r"(taddr)
-      : "memory");
-}
-
 // r[0..15] -> 16 consecutive 32-bit TMEM columns of this thread's lane.
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t *r) {
   asm volatile(
@@ -274,6 +261,65 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm volatile("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// ------------------------------------------------------- packed f32 pairs
+// Two fp32 values in one 64-bit register pair (sm_100 f32x2 arithmetic).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of x in [-125, 8] on the FMA pipe instead of MUFU.
+// Range reduction: adding 1.5*2^23 rounds x to the nearest integer n in the
+// low mantissa bits (t), so f = x - n lies in [-0.5, 0.5]. 2^f comes from a
+// degree-4 polynomial whose coefficients were fitted for this kernel by a
+// Remez exchange on the relative error over [-0.5, 0.5] (max relative error
+// 3.6e-6, far below the 2^-11 rounding of the fp16 P it feeds). 2^n is then
+// applied by adding n << 23 to the bit pattern: t's bits are
+// 0x4B400000 + n, and shifting them left by 23 leaves exactly n << 23.
+// Callers clamp x >= -125 so the result stays a normal fp32.
+__device__ __forceinline__ uint64_t exp2_poly_x2(uint64_t x) {
+  const uint64_t kMagic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t kNegMagic = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t c4 = f2_pack(0.009782912209630013f, 0.009782912209630013f);
+  const uint64_t c3 = f2_pack(0.055976882576942444f, 0.055976882576942444f);
+  const uint64_t c2 = f2_pack(0.24020710587501526f, 0.24020710587501526f);
+  const uint64_t c1 = f2_pack(0.6931136250495911f, 0.6931136250495911f);
+  const uint64_t one = f2_pack(1.0f, 1.0f);
+  const uint64_t neg1 = f2_pack(-1.0f, -1.0f);
+  const uint64_t t = f2_add(x, kMagic);              // n in the low bits
+  const uint64_t n = f2_add(t, kNegMagic);           // n as fp32
+  const uint64_t f = f2_fma(n, neg1, x);             // x - n
+  uint64_t p = f2_fma(f, c4, c3);
+  p = f2_fma(p, f, c2);
+  p = f2_fma(p, f, c1);
+  p = f2_fma(p, f, one);
+  const float2 pf = f2_unpack(p), tf = f2_unpack(t);
+  const float r0 = __int_as_float(__float_as_int(pf.x) + (__float_as_int(tf.x) << 23));
+  const float r1 = __int_as_float(__float_as_int(pf.y) + (__float_as_int(tf.y) << 23));
+  return f2_pack(r0, r1);
 }
 
 // Packs (lo, hi) into an fp16x2 word with round-to-nearest-even; lo lands in
