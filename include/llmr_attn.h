@@ -94,6 +94,15 @@ uint64_t llmr_launch_count(llmr_ctx *ctx);
 int llmr_profile_enable(llmr_ctx *ctx, int on);
 int llmr_profile_read(llmr_ctx *ctx, float *ms2);
 
+/* Failure-detection self-test. Launches one small kernel whose bounded
+ * mbarrier wait can never complete (nothing arrives on the barrier); after
+ * limit_ns it gives up and raises the context's error word, exactly as an
+ * expired wait inside the attention kernel does. The next llmr_sync returns
+ * LLMR_ETIMEOUT and clears the word; the context stays usable. No
+ * counterpart in the reference, whose fence waits are unbounded
+ * (lib/vulkan/compute.c3:156-165). limit_ns must be in (0, 1e9]. */
+int llmr_selftest_wait_timeout(llmr_ctx *ctx, uint64_t limit_ns);
+
 /* Buffers. Replace create_tensor / upload_to_tensor / download_tensor
  * (lib/model/tensor.c3:27-46, :79, :99). upload/download are synchronous,
  * as the reference's staging copies are. */

@@ -7,8 +7,25 @@
 #include <stdint.h>
 
 #include "prologue.cuh"
+#include "ptx.cuh"
 
 namespace llmr {
+
+// Failure-detection probe: one thread waits on an mbarrier that nothing
+// arrives at, through the same bounded wait the attention kernel uses, and
+// raises the error word when the limit expires. The kernel then ends
+// normally, so the context stays usable.
+__global__ void wait_timeout_probe_kernel(int *err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait_for(&bar, 0, &abort_flag, limit_ns)) atomicExch(err, 1);
+}
 
 // batch_head_norm / perhead_rmsnorm mirror: in place on fp32 [S, H*D].
 __global__ void head_norm_f32_kernel(float *data, const float *gain, int H,

@@ -338,6 +338,15 @@ int llmr_sync(llmr_ctx *ctx) {
   return LLMR_OK;
 }
 
+int llmr_selftest_wait_timeout(llmr_ctx *ctx, uint64_t limit_ns) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (limit_ns == 0 || limit_ns > 1000000000ull)
+    return fail(ctx, LLMR_EINVAL, "limit_ns must be in (0, 1e9]");
+  wait_timeout_probe_kernel<<<1, 32, 0, ctx->stream>>>(ctx->d_err, limit_ns);
+  return after_launch(ctx, "wait_timeout_probe");
+}
+
 int llmr_alloc(llmr_ctx *ctx, size_t bytes, void **out) {
   int rc = check_ctx(ctx);
   if (rc) return rc;

@@ -69,8 +69,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Bounded wait for the phase with the given parity to complete. Returns
 // false if the CTA's abort flag was raised (by this wait timing out or by
 // another warp), in which case the caller must stop its role loop.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
-                                          volatile int *abort_flag) {
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t parity,
+                                              volatile int *abort_flag,
+                                              uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
@@ -78,12 +79,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
     if (mbar_try_wait(bar, parity)) return true;
     if ((++n & 63u) == 0) {
       if (*abort_flag) return false;
-      if (globaltimer_ns() - t0 > LLMR_WAIT_LIMIT_NS) {
+      if (globaltimer_ns() - t0 > limit_ns) {
         *abort_flag = 1;
         return false;
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity,
+                                          volatile int *abort_flag) {
+  return mbar_wait_for(bar, parity, abort_flag, LLMR_WAIT_LIMIT_NS);
 }
 
 // Bounded wait that ignores the abort flag; used on the teardown path to

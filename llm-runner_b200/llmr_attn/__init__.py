@@ -86,6 +86,7 @@ def _load() -> ctypes.CDLL:
         "llmr_last_error": (ctypes.c_char_p, [vp]),
         "llmr_sync": (i32, [vp]),
         "llmr_launch_count": (u64, [vp]),
+        "llmr_selftest_wait_timeout": (i32, [vp, u64]),
         "llmr_profile_enable": (i32, [vp, i32]),
         "llmr_profile_read": (i32, [vp, ctypes.POINTER(ctypes.c_float)]),
         "llmr_alloc": (i32, [vp, ctypes.c_size_t, ctypes.POINTER(vp)]),

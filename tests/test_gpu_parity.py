@@ -159,9 +159,10 @@ def test_tc_kernel_ragged_shapes(ctx, D, S):
 
 @pytest.mark.parametrize("D", [64, 128])
 def test_tc_kernel_rescale_paths(ctx, D):
-    """Scores that jump by more than 2^8 (in P) inside later key blocks, at
-    every 32-key chunk position, force the lazy-rescale path: O and the P
-    already written for earlier chunks are rescaled in place."""
+    """Scores that jump inside later key blocks, at different 32-key chunk
+    positions: some jumps stay below the lazy-rescale threshold (P up to
+    2^12.7 against the stale max), the others pass 2^15 and force O and l to
+    be rescaled before P is written."""
     import llmr_attn as L
     torch = _t()
     rng = np.random.default_rng(21 + D)
@@ -171,7 +172,8 @@ def test_tc_kernel_rescale_paths(ctx, D):
     v = rng.standard_normal((B, S, H, D), dtype=np.float32)
     q[..., 0] += 2.0                     # every query shares a component on dim 0
     # (key position, size): block 1 chunk 0, block 2 chunk 1, block 3 chunk 3,
-    # block 4 chunk 2, block 6 chunk 0 -- each jump is well over 8 in log2(P).
+    # block 4 chunk 2, block 6 chunk 0; in log2(P) the jumps are about
+    # +12.7 (no rescale), then +23, +38 and +76 (each a rescale) for D=128.
     for pos, size in ((150, 10.0), (2 * 128 + 40, 60.0), (3 * 128 + 100, 150.0),
                       (4 * 128 + 70, 300.0), (6 * 128 + 5, 600.0)):
         k[0, pos, :, :] = 0.0
@@ -365,3 +367,27 @@ def test_errors_are_reported(ctx):
         L.attention_fused(ctx, big, big, big, ob, L.AttnConfig(n_heads=2, head_dim=128,
                                                                scale=-1.0), batch=1, seq_len=16)
     ctx.sync()
+
+
+def test_bounded_wait_timeout_is_reported(ctx):
+    """A device-side wait that can never complete gives up after its limit;
+    the context reports LLMR_ETIMEOUT at sync and stays usable (failure
+    detection without a GPU fault or hang)."""
+    import llmr_attn as L
+    torch = _t()
+    ctx.sync()
+    ctx.check(L.lib.llmr_selftest_wait_timeout(ctx.handle, 20_000_000))  # 20 ms
+    with pytest.raises(L.LlmrError) as ei:
+        ctx.sync()
+    assert ei.value.status == L.ETIMEOUT
+    ctx.sync()  # the error word was cleared
+    # the context still runs the op correctly
+    rng = np.random.default_rng(9)
+    q = rng.standard_normal((1, 100, 2, 64), dtype=np.float32).astype(np.float16).astype(np.float32)
+    o = torch.empty((1, 100, 128), device="cuda")
+    L.attention_fused(ctx, dev(q).half(), dev(q).half(), dev(q).half(), o,
+                      L.AttnConfig(n_heads=2, head_dim=64, scale=0.125), batch=1, seq_len=100)
+    ctx.sync()
+    check(host(o), oracle_fa(q, q, q, 0.125).reshape(1, 100, 128), what="after timeout")
+    with pytest.raises(L.LlmrError):
+        ctx.check(L.lib.llmr_selftest_wait_timeout(ctx.handle, 0))
