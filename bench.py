@@ -40,6 +40,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-run", action="store_true",
                     help="only W + K fused calls, nothing else (for ncu captures)")
+    ap.add_argument("--mode", choices=["batch", "headsplit", "ring"], default="batch",
+                    help="batch: one batch element per rank (default, weak scaling); "
+                         "headsplit / ring: one attention over all ranks (strong scaling)")
     ap.add_argument("--heads", type=int, default=0,
                     help="with --profile-run: use this many heads (a smaller capture)")
     return ap.parse_args()
@@ -197,6 +200,107 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_strong(args):
+    """One attention of the configuration spread over all ranks (strong
+    scaling): `headsplit` gives each rank a contiguous share of the (b, h)
+    units with no communication; `ring` shards the sequence and passes fp16
+    K/V blocks around the ring with NCCL P2P while each rank computes.
+    Time per step = max over ranks of the CUDA-event time of the call."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.dist import RingAttention, RingOps, head_split_attention
+    from llmr_attn.runner import attn_config, torch_dtype
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    case = C.CASES[args.config]
+    prep = C.prepare(case, L.rope_tables)
+    B, S, H, D = prep.q.shape
+    dt = torch_dtype(case.dtype)
+    dev = f"cuda:{local}"
+    stream = torch.cuda.Stream(device=dev)
+    g32 = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).to(dev)
+    cfg = attn_config(case, S)
+    with torch.cuda.stream(stream):
+        ctx = L.Context(local, stream=stream)
+        qg, kg, cos, sin = g32(prep.q_gain), g32(prep.k_gain), g32(prep.cos), g32(prep.sin)
+        if args.mode == "headsplit":
+            q, k, v = (torch.from_numpy(a).to(dev).to(dt) for a in (prep.q, prep.k, prep.v))
+            o = torch.empty((B, S, H * D), dtype=dt, device=dev)
+            from llmr_attn.dist import partition_units
+            runs = partition_units(B, H, world, rank)
+            need = max(L.workspace_bytes(L.make_desc(L.AttnConfig(**{**cfg.__dict__,
+                                                                     "n_heads": h1 - h0}),
+                                                     1, S, L._dtype_code(q), L._dtype_code(o)))
+                       for _, h0, h1 in runs)
+            ctx.reserve(need)
+            def step():
+                head_split_attention(ctx, q, k, v, o, cfg, batch=B, seq_len=S, rank=rank,
+                                     world=world, q_gain=qg, k_gain=kg, cos=cos, sin=sin)
+            units = sum(h1 - h0 for _, h0, h1 in runs)
+        else:
+            if S % world:
+                raise SystemExit("ring needs seq_len divisible by the number of GPUs")
+            s_loc = S // world
+            sl = slice(rank * s_loc, (rank + 1) * s_loc)
+            q, k, v = (torch.from_numpy(np.ascontiguousarray(a[:, sl])).to(dev).to(dt)
+                       for a in (prep.q, prep.k, prep.v))
+            o = torch.empty((1, s_loc, H * D), dtype=dt, device=dev)
+            ring = RingAttention(RingOps(ctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
+                                 dev)
+            def step():
+                ring.forward(q, k, v, o, qg, kg, cos, sin)
+            units = H
+        for _ in range(max(args.warmup, 3)):
+            step()
+        ctx.sync()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        l0 = ctx.launches
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+        for s_, e_ in ev:
+            s_.record(stream)
+            step()
+            e_.record(stream)
+        torch.cuda.synchronize()
+        ctx.sync()
+        launches = ctx.launches - l0
+    total = torch.tensor([sum(s_.elapsed_time(e_) for s_, e_ in ev)], dtype=torch.float64,
+                         device=dev)
+    if world > 1:
+        dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    ms = float(total.item()) / args.steps
+    value = case.flops / (ms / 1e3) / 1e12
+    peak, _, kind = peaks()
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"{case.name} attention TFLOP/s (whole job, strong scaling)",
+            "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
+            "data": "synthetic", "mode": args.mode,
+            "config": {"workload": case.name, "batch": B, "n_heads": H, "seq_len": S,
+                       "head_dim": D, "units_rank0": units},
+            "pct_of_peak_per_gpu": 100.0 * value / world / peak, "peak_source": kind,
+            "gpu_launches_rank0": launches}), flush=True)
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -204,6 +308,9 @@ def main():
         return
     if args.profile_run:
         profile_run(args)
+        return
+    if args.mode != "batch":
+        run_strong(args)
         return
     import numpy as np
     import torch

@@ -46,9 +46,10 @@ struct FaCfg {
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + NST * TILE_BYTES;
-  // barriers: q_full, kv_full[NST], kv_empty[NST], s_full[2], p_full[2],
-  // o_full, drain ; then tmem base word and abort flag
-  static constexpr int NBAR = 1 + 2 * NST + 2 + 2 + 1 + 1;
+  // barriers: q_full, kv_full[NST], kv_empty[NST], s_full[2],
+  // p_half[2][2] (P of keys 0-63 / 64-127 of tile t written), o_full, drain;
+  // then tmem base word and abort flag
+  static constexpr int NBAR = 1 + 2 * NST + 2 + 4 + 1 + 1;
   static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;  // +align slack
   static constexpr int THREADS = 320;
   static constexpr uint32_t TMEM_COLS = 512;
@@ -137,8 +138,8 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t *kv_full = bars + 1;
   uint64_t *kv_empty = bars + 1 + C::NST;
   uint64_t *s_full = bars + 1 + 2 * C::NST;
-  uint64_t *p_full = s_full + 2;
-  uint64_t *o_full = p_full + 2;
+  uint64_t *p_half = s_full + 2;  // [t * 2 + half]
+  uint64_t *o_full = p_half + 4;
   uint64_t *drain = o_full + 1;
   uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
@@ -159,7 +160,8 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int t = 0; t < 2; t++) {
       mbar_init(&s_full[t], 1);
-      mbar_init(&p_full[t], 4);  // one arrival per softmax warp
+      mbar_init(&p_half[2 * t], 4);  // one arrival per softmax warp
+      mbar_init(&p_half[2 * t + 1], 4);
     }
     mbar_init(o_full, 1);
     mbar_init(drain, 1);
@@ -227,14 +229,25 @@ __global__ void __launch_bounds__(320, 1)
                  sdesc_sw128(ka + off, 16, 1024), IDESC_S, k > 0);
         }
       };
-      auto issue_o = [&](int t, int slot, bool acc) {
+      // O_t (+)= P_t V for the keys of one half of the block (64 keys, four
+      // K=16 steps), as soon as the softmax has written that half of P.
+      auto issue_o_half = [&](int t, int slot, int half, bool acc) {
         const uint32_t va = sKVa + slot * C::TILE_BYTES;
 #pragma unroll
-        for (int k = 0; k < C::BN / 16; k++) {
+        for (int kk = 0; kk < C::BN / 32; kk++) {
+          const int k = half * (C::BN / 32) + kk;
           mma_ts(tmem + C::O_COL + t * D, tmem + t * 128 + k * 8,
                  sdesc_sw128(va + k * 2048, C::CHUNK_BYTES, 1024), IDESC_O,
                  (acc || k > 0) ? 1u : 0u);
         }
+      };
+      auto issue_o = [&](int t, int slot, bool acc, uint32_t parity) {
+        for (int half = 0; half < 2; half++) {
+          if (!mbar_wait(&p_half[2 * t + half], parity, abort_flag)) return false;
+          tc_fence_after();
+          issue_o_half(t, slot, half, acc);
+        }
+        return true;
       };
       bool ok = mbar_wait(q_full, 0, abort_flag);
       if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
@@ -251,18 +264,14 @@ __global__ void __launch_bounds__(320, 1)
         const int uK = 2 * j + 2, sK = uK % C::NST;
         const bool more = j + 1 < nblk;
         if (!mbar_wait(&kv_full[sV], (uV / C::NST) & 1, abort_flag)) break;
-        if (!mbar_wait(&p_full[0], j & 1, abort_flag)) break;
-        tc_fence_after();
-        issue_o(0, sV, j > 0);
+        if (!issue_o(0, sV, j > 0, j & 1)) break;
         if (more) {
           if (!mbar_wait(&kv_full[sK], (uK / C::NST) & 1, abort_flag)) break;
           tc_fence_after();
           issue_s(0, sK);
           mma_commit(&s_full[0]);
         }
-        if (!mbar_wait(&p_full[1], j & 1, abort_flag)) break;
-        tc_fence_after();
-        issue_o(1, sV, j > 0);
+        if (!issue_o(1, sV, j > 0, j & 1)) break;
         mma_commit(&kv_empty[sV]);
         if (more) {
           issue_s(1, sK);
@@ -351,6 +360,14 @@ __global__ void __launch_bounds__(320, 1)
             pk[i] = pack_f16x2(pf.x, pf.y);
           }
           tmem_st16(tS + c * 16, pk);
+          if (c == 1 || c == 3) {
+            // Half of P (keys 0-63, then 64-127) is in TMEM: let the MMA
+            // warp start that half of O += P V while the rest is computed.
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_half[2 * t + (c >> 1)]);
+          }
         }
         const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
         return (s0.x + s0.y) + (s1.x + s1.y);
@@ -378,12 +395,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         m_used = m_tgt;
       }
-      const float l_blk = emit_all();
-      l += l_blk;
-      tmem_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[t]);
+      l += emit_all();
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, abort_flag));
     if (ok) {

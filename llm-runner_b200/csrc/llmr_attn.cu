@@ -157,17 +157,16 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
   const dim3 blocks((pp.S + kProRowsPerCta - 1) / kProRowsPerCta, pp.B * pp.H, 3);
-  // One vector access per lane needs every lane's first element aligned to
-  // E elements: bases aligned and strides multiples of E; tables likewise.
-  constexpr int E = D / 32;
-  auto ok = [&](const void *ptr, const long long *st, size_t bytes) {
+  // 16-byte vector accesses per lane need 16-byte aligned bases and strides
+  // that are whole 16-byte multiples (the tables' rows always are).
+  constexpr int VIN = 16 / sizeof(InT);
+  auto ok = [&](const void *ptr, const long long *st) {
     return ptr == nullptr ||
-           ((reinterpret_cast<uintptr_t>(ptr) % bytes) == 0 &&
-            (st == nullptr || (st[0] % E == 0 && st[1] % E == 0 && st[2] % E == 0)));
+           ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 &&
+            (st == nullptr || (st[0] % VIN == 0 && st[1] % VIN == 0 && st[2] % VIN == 0)));
   };
-  const bool vec = ok(q, qs, sizeof(InT) * E) && ok(k, ks, sizeof(InT) * E) &&
-                   ok(v, vs, sizeof(InT) * E) && ok(pp.cos_t, nullptr, 4 * (E / 2)) &&
-                   ok(pp.sin_t, nullptr, 4 * (E / 2));
+  const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs) && ok(pp.cos_t, nullptr) &&
+                   ok(pp.sin_t, nullptr);
   if (vec)
     prologue_kernel<D, InT, OutT, true><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   else

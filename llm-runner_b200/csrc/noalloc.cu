@@ -124,19 +124,18 @@ template <int D, typename InT>
 int prologue(cudaStream_t st, int num_sms, const void *q, const void *k, const void *v,
              const long long *qs, const long long *ks, const long long *vs, __half *out,
              const ProParams &pp) {
-  constexpr int E = D / 32;
+  constexpr int VIN = 16 / sizeof(InT);
   View<InT> vq{static_cast<const InT *>(q), qs[0], qs[1], qs[2]};
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
   (void)num_sms;
   const dim3 blocks((pp.S + kProRowsPerCta - 1) / kProRowsPerCta, pp.B * pp.H, 3);
-  auto ok = [&](const void *ptr, const long long *s, size_t bytes) {
-    return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) % bytes) == 0 &&
-                              (s == nullptr || (s[0] % E == 0 && s[1] % E == 0 && s[2] % E == 0)));
+  auto ok = [&](const void *ptr, const long long *s) {
+    return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 &&
+                              (s == nullptr || (s[0] % VIN == 0 && s[1] % VIN == 0 && s[2] % VIN == 0)));
   };
-  const bool vec = ok(q, qs, sizeof(InT) * E) && ok(k, ks, sizeof(InT) * E) &&
-                   ok(v, vs, sizeof(InT) * E) && ok(pp.cos_t, nullptr, 4 * (E / 2)) &&
-                   ok(pp.sin_t, nullptr, 4 * (E / 2));
+  const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs) && ok(pp.cos_t, nullptr) &&
+                   ok(pp.sin_t, nullptr);
   if (vec)
     prologue_kernel<D, InT, __half, true><<<blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
   else

@@ -39,100 +39,133 @@ struct alignas(sizeof(T) * N) Pack {
   T v[N];
 };
 
-// Rows per CTA of the prologue: 8 warps x 4 rows in flight per warp.
-constexpr int kProRowsPerWarp = 4;
+// Prologue geometry: a row (one token of one head) is D elements, handled by
+// an 8-lane group with E = D/8 elements per lane, so a warp works on 4 rows
+// at once and the RMSNorm sum needs a 3-step shuffle. A CTA of 8 warps walks
+// kProRowsPerCta rows of one (tensor, b, h).
+constexpr int kProLanesPerRow = 8;
+constexpr int kProRowsPerWarpStep = 32 / kProLanesPerRow;  // 4
 constexpr int kProWarps = 8;
-constexpr int kProRowsPerCta = kProRowsPerWarp * kProWarps;
+constexpr int kProSteps = 4;  // row groups per warp
+constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 128
 
-// Grid (ceil(S / 32), B*H, 3): blockIdx.z selects Q, K or V, blockIdx.y the
-// (b, h) unit, and each warp owns 4 consecutive tokens s of that unit (a
-// row = D elements). Q and K rows get the per-head RMSNorm of
-// batch_head_norm (dependencies/zimage.c3l/shaders/zimage.slang:623-659:
+// Grid (ceil(S / 128), B*H, 3): blockIdx.z selects Q, K or V, blockIdx.y the
+// (b, h) unit. Q and K rows get the per-head RMSNorm of batch_head_norm
+// (dependencies/zimage.c3l/shaders/zimage.slang:623-659:
 // x * (1/sqrt(mean(x^2) + eps)) * g) and the interleaved rotation of mrope
-// (dependencies/zimage.c3l/shaders/mrope.slang:47-53), computed in fp32 with
-// the same operation order; V is only converted. Output: dense
-// [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang applies on
-// load, or fp32 for the exact path). VEC: inputs and tables allow one
-// vector access per lane (checked on the host).
+// (dependencies/zimage.c3l/shaders/mrope.slang:47-53) in fp32, with the
+// shader's operation order for the products; V is only converted. Output:
+// dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
+// applies on load, or fp32 for the exact path). VEC: every lane's slice of
+// the inputs and tables is 16-byte aligned (checked on the host).
 template <int D, typename InT, typename OutT, bool VEC>
 __global__ void __launch_bounds__(256)
     prologue_kernel(View<InT> q, View<InT> k, View<InT> v, OutT *out,
                     ProParams p) {
-  constexpr int E = D / 32;  // elements per lane: 4 (D=128) or 2 (D=64)
-  constexpr int U = kProRowsPerWarp;
+  constexpr int E = D / kProLanesPerRow;  // 16 (D=128) or 8 (D=64)
+  constexpr int VIN = 16 / sizeof(InT);   // elements per 16-byte load
   const int lane = threadIdx.x & 31;
-  const int t = blockIdx.z;  // 0 = Q, 1 = K, 2 = V
+  const int sub = lane & (kProLanesPerRow - 1);  // position inside the row
+  const int t = blockIdx.z;                      // 0 = Q, 1 = K, 2 = V
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
-  const int s0 = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * U;
   // Select by value (a reference into the parameter block would force it
   // into local memory).
   const InT *base = t == 0 ? q.base : (t == 1 ? k.base : v.base);
   const long long bs = t == 0 ? q.bs : (t == 1 ? k.bs : v.bs);
   const long long rs = t == 0 ? q.rs : (t == 1 ? k.rs : v.rs);
   const long long hs = t == 0 ? q.hs : (t == 1 ? k.hs : v.hs);
-  const InT *src0 = base + (long long)b * bs + (long long)h * hs + lane * E;
-  float x[U][E];
+  const InT *src0 = base + (long long)b * bs + (long long)h * hs + sub * E;
+  const float *gain = t == 0 ? p.q_gain : (t == 1 ? p.k_gain : nullptr);
+  const bool rope = t < 2 && p.cos_t != nullptr;
+  OutT *dst0 = out + ((long long)t * p.B * p.H + bh) * (long long)p.S * D + sub * E;
+  const int row_in_warp = lane / kProLanesPerRow;
+  const int s_base = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * kProRowsPerWarpStep +
+                     row_in_warp;
+  // All row groups' loads are issued before any is used, so a warp keeps
+  // kProSteps * 16 * (E / VIN) bytes per lane in flight.
+  Pack<InT, VIN> raw[kProSteps][E / VIN];
 #pragma unroll
-  for (int u = 0; u < U; u++) {
-    if (s0 + u >= p.S) break;
-    const InT *src = src0 + (long long)(s0 + u) * rs;
-    if (VEC) {
-      const Pack<InT, E> pk = *reinterpret_cast<const Pack<InT, E> *>(src);
+  for (int step = 0; step < kProSteps; step++) {
+    const int s = s_base + step * kProRowsPerWarpStep * kProWarps;
+    if (VEC && s < p.S) {
+      const InT *src = src0 + (long long)s * rs;
 #pragma unroll
-      for (int e = 0; e < E; e++) x[u][e] = to_f32<InT>(pk.v[e]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < E; e++) x[u][e] = to_f32<InT>(src[e]);
+      for (int c = 0; c < E / VIN; c++)
+        raw[step][c] = *reinterpret_cast<const Pack<InT, VIN> *>(src + c * VIN);
     }
   }
-  const float *gain = t == 0 ? p.q_gain : (t == 1 ? p.k_gain : nullptr);
-  OutT *dst0 = out + ((long long)t * p.B * p.H + bh) * (long long)p.S * D + lane * E;
 #pragma unroll
-  for (int u = 0; u < U; u++) {
-    const int s = s0 + u;
-    if (s >= p.S) break;
+  for (int step = 0; step < kProSteps; step++) {
+    const int s = s_base + step * kProRowsPerWarpStep * kProWarps;
+    // Lanes of a row group share the row, so the whole 8-lane group is in
+    // or out together; shuffles stay inside the group.
+    const bool in = s < p.S;
+    float x[E];
+    if (in) {
+      if (VEC) {
+#pragma unroll
+        for (int c = 0; c < E / VIN; c++)
+#pragma unroll
+          for (int e = 0; e < VIN; e++) x[c * VIN + e] = to_f32<InT>(raw[step][c].v[e]);
+      } else {
+        const InT *src = src0 + (long long)s * rs;
+#pragma unroll
+        for (int e = 0; e < E; e++) x[e] = to_f32<InT>(src[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < E; e++) x[e] = 0.0f;
+    }
     const long long grow = (long long)p.rope_row_offset + s;  // global token index
     if (gain != nullptr) {
       float ss = 0.0f;
 #pragma unroll
-      for (int e = 0; e < E; e++) ss = __fmaf_rn(x[u][e], x[u][e], ss);
+      for (int e = 0; e < E; e++) ss = __fmaf_rn(x[e], x[e], ss);
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      const float rms = 1.0f / sqrtf(ss / (float)D + p.eps);
-      const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + lane * E;
+      for (int o = kProLanesPerRow / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rms = rsqrtf(ss / (float)D + p.eps);
+      const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + sub * E;
 #pragma unroll
-      for (int e = 0; e < E; e++) x[u][e] = __fmul_rn(__fmul_rn(x[u][e], rms), g[e]);
+      for (int e = 0; e < E; e++) x[e] = __fmul_rn(__fmul_rn(x[e], rms), g[e]);
     }
-    if (t < 2 && p.cos_t != nullptr) {
-      const long long trow = grow * (D / 2) + lane * (E / 2);
+    if (rope && in) {
+      const float *ct = p.cos_t + grow * (D / 2) + sub * (E / 2);
+      const float *st = p.sin_t + grow * (D / 2) + sub * (E / 2);
       float cv[E / 2], sv[E / 2];
       if (VEC) {
-        const Pack<float, E / 2> pc = *reinterpret_cast<const Pack<float, E / 2> *>(p.cos_t + trow);
-        const Pack<float, E / 2> ps = *reinterpret_cast<const Pack<float, E / 2> *>(p.sin_t + trow);
 #pragma unroll
-        for (int e = 0; e < E / 2; e++) {
-          cv[e] = pc.v[e];
-          sv[e] = ps.v[e];
+        for (int c = 0; c < E / 2; c += 4) {
+          const float4 a = *reinterpret_cast<const float4 *>(ct + c);
+          const float4 bq = *reinterpret_cast<const float4 *>(st + c);
+          cv[c] = a.x; cv[c + 1] = a.y; cv[c + 2] = a.z; cv[c + 3] = a.w;
+          sv[c] = bq.x; sv[c + 1] = bq.y; sv[c + 2] = bq.z; sv[c + 3] = bq.w;
         }
       } else {
 #pragma unroll
         for (int e = 0; e < E / 2; e++) {
-          cv[e] = p.cos_t[trow + e];
-          sv[e] = p.sin_t[trow + e];
+          cv[e] = ct[e];
+          sv[e] = st[e];
         }
       }
 #pragma unroll
       for (int e = 0; e < E; e += 2) {
-        const float x0 = x[u][e], x1 = x[u][e + 1];
-        x[u][e] = __fsub_rn(__fmul_rn(x0, cv[e / 2]), __fmul_rn(x1, sv[e / 2]));
-        x[u][e + 1] = __fadd_rn(__fmul_rn(x0, sv[e / 2]), __fmul_rn(x1, cv[e / 2]));
+        const float x0 = x[e], x1 = x[e + 1];
+        x[e] = __fsub_rn(__fmul_rn(x0, cv[e / 2]), __fmul_rn(x1, sv[e / 2]));
+        x[e + 1] = __fadd_rn(__fmul_rn(x0, sv[e / 2]), __fmul_rn(x1, cv[e / 2]));
       }
     }
-    Pack<OutT, E> po;
+    if (in) {
+      constexpr int VOUT = 16 / sizeof(OutT);
+      OutT *dst = dst0 + (long long)s * D;
 #pragma unroll
-    for (int e = 0; e < E; e++) po.v[e] = from_f32<OutT>(x[u][e]);
-    *reinterpret_cast<Pack<OutT, E> *>(dst0 + (long long)s * D) = po;
+      for (int c = 0; c < E / VOUT; c++) {
+        Pack<OutT, VOUT> po;
+#pragma unroll
+        for (int e = 0; e < VOUT; e++) po.v[e] = from_f32<OutT>(x[c * VOUT + e]);
+        *reinterpret_cast<Pack<OutT, VOUT> *>(dst + c * VOUT) = po;
+      }
+    }
   }
 }
 
