@@ -61,7 +61,11 @@ enum {
   LLMR_EXACT = 1u << 3,   /* fp32 operands and exact softmax (spatial_attention
                              math, lib/shaders/diffusion.slang:478-569) instead
                              of fp16 operands (flash_attention_v2 math) */
-  LLMR_LSE = 1u << 4      /* also write log-sum-exp (natural log) per row */
+  LLMR_LSE = 1u << 4,     /* also write log-sum-exp (natural log) per row */
+  LLMR_MERGE = 1u << 5    /* o (fp32) and lse already hold the normalised
+                             result over other keys: merge this call's result
+                             into them by log-sum-exp, in place (the step of
+                             the sequence-sharded ring). Needs LLMR_LSE. */
 };
 
 typedef struct llmr_ctx llmr_ctx;

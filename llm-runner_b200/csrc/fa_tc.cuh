@@ -20,6 +20,8 @@
 // The softmax rescales O lazily: only when a row max grows by more than
 // 2^15 over the max used so far (so fp16 P stays <= 32768).
 #pragma once
+#include <type_traits>
+
 #include "ptx.cuh"
 
 namespace llmr {
@@ -32,6 +34,8 @@ struct FaParams {
   long long o_row_stride;    // elements between consecutive tokens
   long long o_batch_stride;  // elements between batch elements
   float *lse;            // optional [B][H][S] natural-log LSE
+  int merge;             // o (fp32) and lse hold a partial result over other
+                         // keys: merge into them by log-sum-exp
   int *err;              // device error word (nonzero on timeout)
 };
 
@@ -401,9 +405,24 @@ __global__ void __launch_bounds__(320, 1)
     if (ok) {
       tc_fence_after();
       const int qrow = q0 + t * C::BM + row;
-      const float inv_l = 1.0f / l;
       OutT *dst = reinterpret_cast<OutT *>(p.o) + (long long)b * p.o_batch_stride +
                   (long long)qrow * p.o_row_stride + (long long)h * D;
+      const float lse_t = (m_used + log2f(l)) * 0.69314718055994531f;
+      // o = a * prev + c * acc: a = 0, c = 1/l normally; with merge, the
+      // log-sum-exp weights of the previous partial result (over other
+      // keys, read from o and lse in place) and of this one.
+      float ca = 0.0f, ct = 1.0f / l, lse_out = lse_t;
+      constexpr bool kCanMerge = std::is_same<OutT, float>::value;
+      const bool merge = kCanMerge && p.merge && qrow < S;
+      if (merge) {
+        const float la = p.lse[(long long)bh * S + qrow];
+        const float mx = fmaxf(la, lse_t);
+        const float wa = expf(la - mx), wt = expf(lse_t - mx);
+        const float inv = 1.0f / (wa + wt);
+        ca = wa * inv;
+        ct = wt * inv / l;
+        lse_out = mx + logf(wa + wt);
+      }
 #pragma unroll
       for (int c = 0; c < D / 32; c++) {
         uint32_t o[32];
@@ -412,11 +431,22 @@ __global__ void __launch_bounds__(320, 1)
         reg_fence32(o);
         float v[32];
 #pragma unroll
-        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[i]) * inv_l;
+        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[i]) * ct;
+        if constexpr (kCanMerge) {
+          if (merge) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4) {
+              const float4 pv = *reinterpret_cast<const float4 *>(dst + c * 32 + i);
+              v[i] = fmaf(pv.x, ca, v[i]);
+              v[i + 1] = fmaf(pv.y, ca, v[i + 1]);
+              v[i + 2] = fmaf(pv.z, ca, v[i + 2]);
+              v[i + 3] = fmaf(pv.w, ca, v[i + 3]);
+            }
+          }
+        }
         if (qrow < S) store_row_chunk<OutT>(dst + c * 32, v);
       }
-      if (p.lse != nullptr && qrow < S)
-        p.lse[(long long)bh * S + qrow] = (m_used + log2f(l)) * 0.69314718055994531f;
+      if (p.lse != nullptr && qrow < S) p.lse[(long long)bh * S + qrow] = lse_out;
     }
   }
 

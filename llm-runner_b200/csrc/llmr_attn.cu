@@ -113,7 +113,7 @@ int make_map(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S,
 template <int D, typename OutT>
 int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                  const CUtensorMap &mv, int B, int H, int S, float scale, void *o,
-                 long long o_rs, long long o_bs, float *lse) {
+                 long long o_rs, long long o_bs, float *lse, int merge) {
   using C = FaCfg<D>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -130,6 +130,7 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   p.o_row_stride = o_rs;
   p.o_batch_stride = o_bs;
   p.lse = lse;
+  p.merge = merge;
   p.err = ctx->d_err;
   dim3 grid((S + 2 * C::BM - 1) / (2 * C::BM), B * H);
   fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
@@ -138,15 +139,16 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
 
 int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
                      const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S,
-                     float scale, void *o, long long o_rs, long long o_bs, float *lse) {
+                     float scale, void *o, long long o_rs, long long o_bs, float *lse,
+                     int merge) {
   if (D == 128) {
-    if (od == LLMR_F32) return launch_fa_tc<128, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
-    if (od == LLMR_F16) return launch_fa_tc<128, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
-    return launch_fa_tc<128, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+    if (od == LLMR_F32) return launch_fa_tc<128, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, merge);
+    if (od == LLMR_F16) return launch_fa_tc<128, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
+    return launch_fa_tc<128, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
   }
-  if (od == LLMR_F32) return launch_fa_tc<64, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
-  if (od == LLMR_F16) return launch_fa_tc<64, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
-  return launch_fa_tc<64, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse);
+  if (od == LLMR_F32) return launch_fa_tc<64, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, merge);
+  if (od == LLMR_F16) return launch_fa_tc<64, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
+  return launch_fa_tc<64, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
 }
 
 template <int D, typename InT, typename OutT>
@@ -402,6 +404,9 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
   if ((d->flags & LLMR_NORM_K) && !k_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_K needs k_gain");
   if ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) return fail(ctx, LLMR_EINVAL, "LLMR_ROPE needs cos/sin tables");
   if ((d->flags & LLMR_LSE) && !lse) return fail(ctx, LLMR_EINVAL, "LLMR_LSE needs an lse buffer");
+  if ((d->flags & LLMR_MERGE) &&
+      (!(d->flags & LLMR_LSE) || d->out_dtype != LLMR_F32 || (d->flags & LLMR_EXACT)))
+    return fail(ctx, LLMR_EINVAL, "LLMR_MERGE needs LLMR_LSE, an fp32 output and the tensor-core path");
   const bool exact = d->flags & LLMR_EXACT;
   if (exact && d->out_dtype != LLMR_F32) return fail(ctx, LLMR_EINVAL, "LLMR_EXACT writes fp32 output");
   const size_t need = llmr_attention_workspace_bytes(d);
@@ -477,7 +482,7 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
   }
   mark(1);
   rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o, o_rs, o_bs,
-                        lse_out);
+                        lse_out, (d->flags & LLMR_MERGE) ? 1 : 0);
   mark(2);
   ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
   return rc;

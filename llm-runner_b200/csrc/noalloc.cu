@@ -164,6 +164,7 @@ int attention(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, con
   p.o_row_stride = o_rs;
   p.o_batch_stride = o_bs;
   p.lse = lse;
+  p.merge = 0;
   p.err = err;
   dim3 grid((S + 2 * C::BM - 1) / (2 * C::BM), B * H);
   fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(mq, mk, mv, p);
@@ -201,7 +202,7 @@ extern "C" int llmr_attention_fused_noalloc(const llmr_attn_desc *d, const void 
     return LLMR_EINVAL;
   if (d->in_dtype > LLMR_BF16 || d->out_dtype > LLMR_BF16 || d->layout > LLMR_LAYOUT_BHSD)
     return LLMR_EINVAL;
-  if (d->flags & LLMR_EXACT) return LLMR_EINVAL;  // tensor-core path only
+  if (d->flags & (LLMR_EXACT | LLMR_MERGE)) return LLMR_EINVAL;  // plain tensor-core path only
   if (((d->flags & LLMR_NORM_Q) && !q_gain) || ((d->flags & LLMR_NORM_K) && !k_gain) ||
       ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) || ((d->flags & LLMR_LSE) && !lse))
     return LLMR_EINVAL;

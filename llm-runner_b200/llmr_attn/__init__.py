@@ -39,7 +39,7 @@ _STATUS_NAMES = {0: "LLMR_OK", 1: "LLMR_EINVAL", 2: "LLMR_ENOMEM", 3: "LLMR_ECUD
 
 F32, F16, BF16 = 0, 1, 2
 BSHD, BHSD = 0, 1
-NORM_Q, NORM_K, ROPE, EXACT, LSE = 1, 2, 4, 8, 16
+NORM_Q, NORM_K, ROPE, EXACT, LSE, MERGE = 1, 2, 4, 8, 16, 32
 
 
 class LlmrError(RuntimeError):
@@ -276,13 +276,14 @@ class AttnConfig:
 
 
 def make_desc(cfg: AttnConfig, batch: int, seq_len: int, in_dtype: int, out_dtype: int,
-              lse: bool = False, strides: Optional[dict] = None) -> AttnDesc:
+              lse: bool = False, strides: Optional[dict] = None,
+              merge: bool = False) -> AttnDesc:
     d = AttnDesc()
     d.batch, d.n_heads, d.seq_len, d.head_dim = batch, cfg.n_heads, seq_len, cfg.head_dim
     d.in_dtype, d.out_dtype, d.layout = in_dtype, out_dtype, cfg.layout
     d.flags = ((NORM_Q if cfg.norm_q else 0) | (NORM_K if cfg.norm_k else 0)
                | (ROPE if cfg.rope else 0) | (EXACT if cfg.exact else 0)
-               | (LSE if lse else 0))
+               | (LSE if lse else 0) | (MERGE if merge else 0))
     d.scale, d.eps = cfg.scale, cfg.eps
     d.split_row, d.rope_row_offset = cfg.split_row, cfg.rope_row_offset
     for key, val in (strides or {}).items():
@@ -296,14 +297,16 @@ def workspace_bytes(desc: AttnDesc) -> int:
 
 def attention_fused(ctx: Context, q, k, v, o, cfg: AttnConfig, *, batch: int, seq_len: int,
                     q_gain=None, k_gain=None, cos=None, sin=None, lse=None,
-                    strides: Optional[dict] = None) -> None:
+                    strides: Optional[dict] = None, merge: bool = False) -> None:
     """Fused QK-RMSNorm + RoPE + non-causal attention into `o` [B,S,H*D].
 
     q/k/v: torch CUDA tensors (f32/f16/bf16) in cfg.layout; gains fp32
     [D] or [2,D] (txt/img split at cfg.split_row); cos/sin fp32 [rows, D/2].
+    merge: o (fp32) and lse already hold a result over other keys; this
+    call's result is merged into them by log-sum-exp.
     """
     desc = make_desc(cfg, batch, seq_len, _dtype_code(q), _dtype_code(o),
-                     lse=lse is not None, strides=strides)
+                     lse=lse is not None, strides=strides, merge=merge)
     ctx.check(lib.llmr_attention_fused(ctx.handle, ctypes.byref(desc), _ptr(q), _ptr(k),
                                        _ptr(v), _ptr(q_gain), _ptr(k_gain), _ptr(cos),
                                        _ptr(sin), _ptr(o), _ptr(lse)))

@@ -15,6 +15,7 @@ Two schemes, both new relative to the reference (which is single-GPU,
   merged into the running result by log-sum-exp, while the block is passed
   to rank r+1 and the next one received from rank r-1 by NCCL P2P
   (batch_isend_irecv) on NCCL's stream, overlapping the attention kernel.
+  The merge happens in the attention kernel's epilogue (LLMR_MERGE).
   `RingAttention`.
 
 The ring's schedule and merge are plain host logic over pluggable ops, so
@@ -74,7 +75,7 @@ def head_split_attention(ctx: "L.Context", q, k, v, o, cfg: "L.AttnConfig", *, b
 # ---------------------------------------------------------------------- ring
 
 class RingOps:
-    """The four device steps of the ring, on the library's CUDA kernels."""
+    """The device steps of the ring, on the library's CUDA kernels."""
 
     def __init__(self, ctx: "L.Context", cfg: "L.AttnConfig", seq_local: int,
                  row_offset: int):
@@ -91,13 +92,12 @@ class RingOps:
         L.attention_prologue(self.ctx, q, k, v, qkv_out, pc, batch=1, seq_len=self.S,
                              q_gain=q_gain, k_gain=k_gain, cos=cos, sin=sin)
 
-    def partial(self, qh, kh, vh, o, lse):
+    def partial(self, qh, kh, vh, o, lse, merge):
+        """Attention of this rank's Q against one K/V block into (o, lse);
+        with merge, folded into the result already there (log-sum-exp merge
+        in the kernel's epilogue)."""
         L.attention_fused(self.ctx, qh, kh, vh, o, self.part_cfg, batch=1, seq_len=self.S,
-                          lse=lse)
-
-    def merge(self, o_acc, lse_acc, o_t, lse_t):
-        L.attention_merge(self.ctx, o_acc, lse_acc, o_t, lse_t, self.S, self.cfg.n_heads,
-                          self.cfg.head_dim)
+                          lse=lse, merge=merge)
 
     def finalize(self, o_acc, out):
         L.convert_f32(self.ctx, o_acc, out)
@@ -109,8 +109,6 @@ class RingBuffers:
     kv_nxt: object   # fp16 [2, H, S_loc, D] (receive buffer)
     o_acc: object    # fp32 [S_loc, H*D]
     lse_acc: object  # fp32 [H, S_loc]
-    o_tmp: object
-    lse_tmp: object
 
 
 class RingAttention:
@@ -129,9 +127,7 @@ class RingAttention:
             qkv=ops.empty((3, H, S, D), dt, device),
             kv_nxt=ops.empty((2, H, S, D), dt, device),
             o_acc=ops.empty((S, H * D), torch.float32, device),
-            lse_acc=ops.empty((H, S), torch.float32, device),
-            o_tmp=ops.empty((S, H * D), torch.float32, device),
-            lse_tmp=ops.empty((H, S), torch.float32, device))
+            lse_acc=ops.empty((H, S), torch.float32, device))
 
     def forward(self, q, k, v, out, q_gain=None, k_gain=None, cos=None, sin=None) -> None:
         """q/k/v: this rank's token shard [1, S_loc, H, D]; out: [1, S_loc, H*D]."""
@@ -148,11 +144,7 @@ class RingAttention:
                 reqs = dist.batch_isend_irecv([
                     dist.P2POp(dist.isend, kv_cur, nxt_rank, self.group),
                     dist.P2POp(dist.irecv, kv_nxt, prv_rank, self.group)])
-            if t == 0:
-                self.ops.partial(qh, kv_cur[0], kv_cur[1], b.o_acc, b.lse_acc)
-            else:
-                self.ops.partial(qh, kv_cur[0], kv_cur[1], b.o_tmp, b.lse_tmp)
-                self.ops.merge(b.o_acc, b.lse_acc, b.o_tmp, b.lse_tmp)
+            self.ops.partial(qh, kv_cur[0], kv_cur[1], b.o_acc, b.lse_acc, merge=t > 0)
             if reqs is not None:
                 for w in reqs:
                     w.wait()

@@ -52,24 +52,24 @@ class CpuRingOps:
         for i, t in enumerate((q, k, v)):
             qkv_out[i] = t[0].permute(1, 0, 2).to(torch.float64)
 
-    def partial(self, qh, kh, vh, o, lse):
+    def partial(self, qh, kh, vh, o, lse, merge):
         s = torch.einsum("hsd,htd->hst", qh, kh) * self.scale
         m = s.amax(-1, keepdim=True)
         p = torch.exp(s - m)
         l = p.sum(-1, keepdim=True)
-        lse.copy_((m + torch.log(l))[..., 0])
-        oh = torch.einsum("hst,htd->hsd", p / l, vh)      # [H, S, D]
-        o.copy_(oh.permute(1, 0, 2).reshape(o.shape))
-
-    def merge(self, o_acc, lse_acc, o_t, lse_t):
-        H, D = self.H, self.D
-        S = o_acc.shape[0]
-        mx = torch.maximum(lse_acc, lse_t)
-        wa, wb = torch.exp(lse_acc - mx), torch.exp(lse_t - mx)      # [H, S]
-        oa, ob = o_acc.view(S, H, D), o_t.view(S, H, D)
+        lse_t = (m + torch.log(l))[..., 0]
+        o_t = torch.einsum("hst,htd->hsd", p / l, vh).permute(1, 0, 2).reshape(o.shape)
+        if not merge:
+            o.copy_(o_t)
+            lse.copy_(lse_t)
+            return
+        H, D, S = self.H, self.D, o.shape[0]
+        mx = torch.maximum(lse, lse_t)
+        wa, wb = torch.exp(lse - mx), torch.exp(lse_t - mx)      # [H, S]
+        oa, ob = o.view(S, H, D), o_t.view(S, H, D)
         waT, wbT = wa.t()[..., None], wb.t()[..., None]
         oa.copy_((waT * oa + wbT * ob) / (waT + wbT))
-        lse_acc.copy_(mx + torch.log(wa + wb))
+        lse.copy_(mx + torch.log(wa + wb))
 
     def finalize(self, o_acc, out):
         out.copy_(o_acc.view(out.shape))

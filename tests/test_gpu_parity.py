@@ -283,6 +283,53 @@ def test_lse_output(ctx):
     assert np.abs(host(lse)[0] - want).max() < 1e-3
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_merge_flag_combines_key_blocks(ctx, D):
+    """LLMR_MERGE: attention over key block A, then over key block B merged
+    into the same fp32 O / LSE, equals attention over the keys of A and B
+    together (as the ring does with one block per step). Block B has a much
+    larger logit range, so the merge weights are far from 1/2; S is not a
+    tile multiple."""
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(D)
+    S, H = 333, 2
+    q = rng.standard_normal((S, H, D)).astype(np.float16).astype(np.float32)
+    k = rng.standard_normal((2, S, H, D)).astype(np.float16).astype(np.float32)
+    k[1] = (k[1] * 3.0).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((2, S, H, D)).astype(np.float16).astype(np.float32)
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=D ** -0.5, layout=L.BHSD)
+
+    def bhsd(x):
+        return dev(x.transpose(1, 0, 2)).half().contiguous()
+
+    qh = bhsd(q)
+    o = torch.empty((S, H * D), device="cuda")
+    lse = torch.empty((H, S), device="cuda")
+    for i in range(2):
+        L.attention_fused(ctx, qh, bhsd(k[i]), bhsd(v[i]), o, cfg, batch=1, seq_len=S,
+                          lse=lse, merge=i > 0)
+    ctx.sync()
+    kk = np.concatenate([k[0], k[1]], 0).astype(np.float64)
+    vv = np.concatenate([v[0], v[1]], 0).astype(np.float64)
+    s = np.einsum("shd,thd->hst", q.astype(np.float64), kk) * D ** -0.5
+    mx = s.max(-1, keepdims=True)
+    p = np.exp(s - mx)
+    want_lse = (mx + np.log(p.sum(-1, keepdims=True)))[..., 0]
+    want = np.einsum("hst,thd->shd", p / p.sum(-1, keepdims=True), vv).reshape(S, H * D)
+    check(host(o), want, what=f"merge D={D}")
+    assert np.abs(host(lse) - want_lse).max() < 1e-3
+    # misuse: merge into a non-fp32 output, or without LSE, is rejected
+    o16 = torch.empty((S, H * D), device="cuda", dtype=torch.float16)
+    kh = bhsd(k[0])
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_fused(ctx, qh, kh, kh, o16, cfg, batch=1, seq_len=S, lse=lse, merge=True)
+    assert ei.value.status == L.EINVAL
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_fused(ctx, qh, kh, kh, o, cfg, batch=1, seq_len=S, merge=True)
+    assert ei.value.status == L.EINVAL
+
+
 # ----------------------------------------------------------------- configurations
 
 def _run_case(ctx, case, rows_windows=None, **over):

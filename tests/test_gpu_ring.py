@@ -1,8 +1,8 @@
 """GPU: the sequence-sharded ring (dependencies of RingAttention).
 
 test_ring_ops_emulated runs every virtual rank's steps in one process on one
-GPU (shard prologue with global RoPE rows and global gain split, partial
-attention with LSE, LSE merge, final conversion) and checks each shard of O
+GPU (shard prologue with global RoPE rows and global gain split, attention
+with LSE merged in the kernel epilogue, final conversion) and checks each shard of O
 against the oracle on the whole sequence. test_ring_nccl runs the real ring
 (NCCL P2P between processes) and needs two GPUs; it is skipped on one."""
 import os
@@ -56,14 +56,9 @@ def test_ring_ops_emulated(ctx, P):
         ops, buf = qkv[r]
         o_acc = torch.empty((s_loc, H * D), device="cuda")
         l_acc = torch.empty((H, s_loc), device="cuda")
-        o_t, l_t = torch.empty_like(o_acc), torch.empty_like(l_acc)
         for t in range(P):
             src = qkv[(r - t) % P][1]
-            if t == 0:
-                ops.partial(buf[0], src[1], src[2], o_acc, l_acc)
-            else:
-                ops.partial(buf[0], src[1], src[2], o_t, l_t)
-                ops.merge(o_acc, l_acc, o_t, l_t)
+            ops.partial(buf[0], src[1], src[2], o_acc, l_acc, merge=t > 0)
         out = torch.empty((1, s_loc, H * D), device="cuda", dtype=torch.float32)
         ops.finalize(o_acc, out)
         ctx.sync()
