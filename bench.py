@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--mode", choices=["batch", "headsplit", "ring"], default="batch",
                     help="batch: one batch element per rank (default, weak scaling); "
                          "headsplit / ring: one attention over all ranks (strong scaling)")
+    ap.add_argument("--transport", choices=["copy", "nccl"], default="copy",
+                    help="ring mode: K/V blocks pulled from their owners on the copy engines "
+                         "(copy) or passed around the ring by NCCL P2P (nccl)")
     ap.add_argument("--heads", type=int, default=0,
                     help="with --profile-run: use this many heads (a smaller capture)")
     return ap.parse_args()
@@ -203,8 +206,9 @@ def run_reference(args):
 def run_strong(args):
     """One attention of the configuration spread over all ranks (strong
     scaling): `headsplit` gives each rank a contiguous share of the (b, h)
-    units with no communication; `ring` shards the sequence and passes fp16
-    K/V blocks around the ring with NCCL P2P while each rank computes.
+    units with no communication; `ring` shards the sequence and moves the
+    fp16 K/V blocks between ranks (copy engines or NCCL P2P, --transport)
+    while each rank computes.
     Time per step = max over ranks of the CUDA-event time of the call."""
     import numpy as np
     import torch
@@ -257,7 +261,7 @@ def run_strong(args):
                        for a in (prep.q, prep.k, prep.v))
             o = torch.empty((1, s_loc, H * D), dtype=dt, device=dev)
             ring = RingAttention(RingOps(ctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
-                                 dev)
+                                 dev, transport=args.transport)
             def step():
                 ring.forward(q, k, v, o, qg, kg, cos, sin)
             units = H
@@ -291,10 +295,16 @@ def run_strong(args):
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
             "data": "synthetic", "mode": args.mode,
+            "transport": args.transport if args.mode == "ring" else None,
             "config": {"workload": case.name, "batch": B, "n_heads": H, "seq_len": S,
                        "head_dim": D, "units_rank0": units},
             "pct_of_peak_per_gpu": 100.0 * value / world / peak, "peak_source": kind,
             "gpu_launches_rank0": launches}), flush=True)
+    if args.mode == "ring":
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        ring.close()
     ctx.close()
     if world > 1:
         dist.barrier()

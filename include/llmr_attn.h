@@ -117,6 +117,26 @@ int llmr_upload(llmr_ctx *ctx, void *dst_device, const void *src_host,
 int llmr_download(llmr_ctx *ctx, void *dst_host, const void *src_device,
                   size_t bytes);
 
+/* Peer buffers for the sequence-sharded attention across GPUs (one process
+ * per GPU). No counterpart in the reference, which runs on one GPU
+ * (docs/flux_server.md:84-88). A buffer from llmr_alloc (the allocation's
+ * base address) is exported as an opaque handle, sent to the other
+ * processes by the caller (any host channel), and mapped there with
+ * llmr_ipc_open. llmr_copy_async moves bytes between the GPUs on the copy
+ * engines over NVLink, using no SMs, so the transfer of the next K/V block
+ * overlaps the attention kernel. The caller orders copies against the
+ * owner's writes (e.g. a barrier after the owner's prologue). */
+typedef struct {
+  unsigned char bytes[64];
+} llmr_ipc_handle;
+int llmr_ipc_export(llmr_ctx *ctx, void *base, llmr_ipc_handle *out);
+int llmr_ipc_open(llmr_ctx *ctx, const llmr_ipc_handle *handle, void **out);
+int llmr_ipc_close(llmr_ctx *ctx, void *mapped);
+/* cudaMemcpyAsync(dst, src, bytes, default kind) on `stream` (NULL = the
+ * context's stream). */
+int llmr_copy_async(llmr_ctx *ctx, void *dst, const void *src, size_t bytes,
+                    void *stream);
+
 /* ---- Mirrors of the reference's attention ops (fp32 buffers) ---------- */
 
 /* flash_attention_v2 (dependencies/zimage.c3l/shaders/flash_attn.slang:38-241;

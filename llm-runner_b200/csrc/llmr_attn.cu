@@ -380,6 +380,46 @@ int llmr_download(llmr_ctx *ctx, void *dst, const void *src, size_t bytes) {
   return LLMR_OK;
 }
 
+static_assert(sizeof(llmr_ipc_handle) == sizeof(cudaIpcMemHandle_t), "ipc handle size");
+
+int llmr_ipc_export(llmr_ctx *ctx, void *base, llmr_ipc_handle *out) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!base || !out) return fail(ctx, LLMR_EINVAL, "null pointer");
+  cudaIpcMemHandle_t h;
+  CUDA_TRY(ctx, cudaIpcGetMemHandle(&h, base));
+  memcpy(out->bytes, &h, sizeof(h));
+  return LLMR_OK;
+}
+
+int llmr_ipc_open(llmr_ctx *ctx, const llmr_ipc_handle *handle, void **out) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!handle || !out) return fail(ctx, LLMR_EINVAL, "null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle->bytes, sizeof(h));
+  CUDA_TRY(ctx, cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess));
+  return LLMR_OK;
+}
+
+int llmr_ipc_close(llmr_ctx *ctx, void *mapped) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!mapped) return fail(ctx, LLMR_EINVAL, "null pointer");
+  CUDA_TRY(ctx, cudaIpcCloseMemHandle(mapped));
+  return LLMR_OK;
+}
+
+int llmr_copy_async(llmr_ctx *ctx, void *dst, const void *src, size_t bytes, void *stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (bytes == 0) return LLMR_OK;
+  if (!dst || !src) return fail(ctx, LLMR_EINVAL, "null pointer");
+  cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+  CUDA_TRY(ctx, cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDefault, s));
+  return LLMR_OK;
+}
+
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {
   if (!d) return 0;
   const size_t n = (size_t)d->batch * d->n_heads * d->seq_len * d->head_dim;

@@ -69,6 +69,11 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class IpcHandle(ctypes.Structure):
+    """llmr_ipc_handle: an exported device allocation (64 opaque bytes)."""
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
 def _load() -> ctypes.CDLL:
     if not os.path.exists(LIB_PATH):
         raise ImportError(
@@ -110,6 +115,10 @@ def _load() -> ctypes.CDLL:
         "llmr_attention_fused_noalloc": (i32, [ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                                vp, vp, vp, vp, vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
+        "llmr_ipc_export": (i32, [vp, vp, ctypes.POINTER(IpcHandle)]),
+        "llmr_ipc_open": (i32, [vp, ctypes.POINTER(IpcHandle), ctypes.POINTER(vp)]),
+        "llmr_ipc_close": (i32, [vp, vp]),
+        "llmr_copy_async": (i32, [vp, vp, vp, ctypes.c_size_t, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -359,6 +368,75 @@ def attention_merge(ctx: Context, o_a, lse_a, o_b, lse_b, rows: int, n_heads: in
                                        _ptr(lse_b), rows, n_heads, head_dim, o_row_stride))
 
 
+# --------------------------------------------------------------------- peer buffers
+
+_TYPESTR = {"float16": "<f2", "bfloat16": None, "float32": "<f4", "uint8": "|u1"}
+
+
+class DeviceBuffer:
+    """A device allocation of its own (llmr_alloc), as IPC export needs, with
+    torch views of it. Freed by close()."""
+
+    def __init__(self, ctx: Context, nbytes: int):
+        p = ctypes.c_void_p()
+        ctx.check(lib.llmr_alloc(ctx.handle, nbytes, ctypes.byref(p)))
+        self.ctx, self.ptr, self.nbytes = ctx, p.value, nbytes
+
+    def tensor(self, shape, dtype):
+        """A torch tensor over the whole buffer (dense, `shape`, `dtype`)."""
+        import torch
+        name = str(dtype).replace("torch.", "")
+        n = int(np.prod(shape)) * torch.empty((), dtype=dtype).element_size()
+        if _TYPESTR.get(name) is None or n > self.nbytes:
+            raise LlmrError(EINVAL, f"cannot view {self.nbytes} bytes as {shape} {dtype}")
+        view = _CudaArray(self.ptr, tuple(int(x) for x in shape), _TYPESTR[name])
+        return torch.as_tensor(view, device=f"cuda:{self.ctx.device}")
+
+    def export(self) -> bytes:
+        h = IpcHandle()
+        self.ctx.check(lib.llmr_ipc_export(self.ctx.handle, ctypes.c_void_p(self.ptr),
+                                           ctypes.byref(h)))
+        return bytes(h.bytes)
+
+    def close(self) -> None:
+        if self.ptr:
+            self.ctx.check(lib.llmr_free(self.ctx.handle, ctypes.c_void_p(self.ptr)))
+            self.ptr = None
+
+
+class _CudaArray:
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape,
+                                         "typestr": typestr, "version": 2}
+
+
+class PeerMapping:
+    """Another process's DeviceBuffer mapped into this one (llmr_ipc_open):
+    `ptr` is readable by copies on this GPU."""
+
+    def __init__(self, ctx: Context, handle: bytes):
+        h = IpcHandle()
+        ctypes.memmove(h.bytes, handle, 64)
+        p = ctypes.c_void_p()
+        ctx.check(lib.llmr_ipc_open(ctx.handle, ctypes.byref(h), ctypes.byref(p)))
+        self.ctx, self.ptr = ctx, p.value
+
+    def close(self) -> None:
+        if self.ptr:
+            self.ctx.check(lib.llmr_ipc_close(self.ctx.handle, ctypes.c_void_p(self.ptr)))
+            self.ptr = None
+
+
+def copy_async(ctx: Context, dst: int, src: int, nbytes: int, stream=None) -> None:
+    """nbytes from address src to address dst on `stream` (copy engines; any
+    two GPUs of the process, peer mappings included)."""
+    raw = None
+    if stream is not None:
+        raw = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+    ctx.check(lib.llmr_copy_async(ctx.handle, ctypes.c_void_p(dst), ctypes.c_void_p(src),
+                                  nbytes, ctypes.c_void_p(raw or None)))
+
+
 # ------------------------------------------------------------------- host helpers
 
 def rope_tables(pos: np.ndarray, axes_dims: Sequence[int], theta: float):
@@ -385,5 +463,6 @@ __all__ = [
     "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
     "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
     "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
-    "rope_tables", "LIB_PATH", "lib",
+    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "IpcHandle", "LIB_PATH",
+    "lib",
 ]

@@ -8,15 +8,22 @@ Two schemes, both new relative to the reference (which is single-GPU,
   [r*U/N, (r+1)*U/N) straight from strided views of the full tensors and
   writes its slice of O. `partition_units` / `head_split_attention`.
 
-* Sequence-sharded ring for long sequences. Rank r holds tokens
+* Sequence-sharded attention for long sequences. Rank r holds tokens
   [r*S/P, (r+1)*S/P). It normalises and rotates its own Q/K once (global
-  RoPE rows and global txt/img gain split), then runs P steps: attention of
-  its Q against the K/V block it currently holds (fp32 partial O + LSE),
-  merged into the running result by log-sum-exp, while the block is passed
-  to rank r+1 and the next one received from rank r-1 by NCCL P2P
-  (batch_isend_irecv) on NCCL's stream, overlapping the attention kernel.
-  The merge happens in the attention kernel's epilogue (LLMR_MERGE).
-  `RingAttention`.
+  RoPE rows and global txt/img gain split), then runs P steps; in step t it
+  attends with its Q to the K/V block of rank (r - t) mod P (fp32 partial O
+  + LSE), merged into the running result by log-sum-exp in the attention
+  kernel's epilogue (LLMR_MERGE). `RingAttention`, with two transports for
+  the K/V blocks:
+  - "copy": every rank exports its fp16 Q/K/V block (CUDA IPC) once; after
+    a barrier that follows all prologues, each rank pulls the P-1 other
+    blocks straight from their owners on the copy engines, in step order,
+    on a side stream, while the attention kernel runs on all SMs. NVSwitch
+    gives every pair full bandwidth, so no block is passed on hop by hop.
+    A second barrier after the pulls lets owners overwrite their block in
+    the next call.
+  - "nccl": the classic ring: the current block goes to rank r+1 and the
+    next one comes from rank r-1 by NCCL P2P (batch_isend_irecv) each step.
 
 The ring's schedule and merge are plain host logic over pluggable ops, so
 they are exercised on CPU with gloo ranks as well as on GPUs with NCCL.
@@ -102,6 +109,78 @@ class RingOps:
     def finalize(self, o_acc, out):
         L.convert_f32(self.ctx, o_acc, out)
 
+    # -- "copy" transport: peer blocks on the copy engines ----------------------
+
+    def share(self, shape, dtype, device, rank, world, group):
+        """Allocates this rank's Q/K/V block as an exportable buffer and maps
+        every other rank's (collective over `group`)."""
+        import torch
+        import torch.distributed as dist
+        n = 1
+        for x in shape:
+            n *= int(x)
+        esize = torch.empty((), dtype=dtype).element_size()
+        self.own = L.DeviceBuffer(self.ctx, n * esize)
+        handles = [None] * world
+        dist.all_gather_object(handles, self.own.export(), group=group)
+        self.peers = [None if r == rank else L.PeerMapping(self.ctx, handles[r])
+                      for r in range(world)]
+        self.kv_offset = (n // shape[0]) * esize          # bytes of the Q part
+        self.kv_bytes = 2 * self.kv_offset
+        self.group = group
+        self.compute = torch.cuda.current_stream()
+        self.comm = torch.cuda.Stream()
+        self.tok = torch.zeros(1, device=device)
+        self.released = None
+        return self.own.tensor(shape, dtype)
+
+    def _barrier_on_comm(self):
+        import torch
+        import torch.distributed as dist
+        with torch.cuda.stream(self.comm):
+            dist.all_reduce(self.tok, group=self.group)
+
+    def wait_released(self):
+        """The compute stream waits until every rank has finished reading this
+        rank's block of the previous call."""
+        if self.released is not None:
+            self.compute.wait_event(self.released)
+
+    def sync_peers(self):
+        """Barrier (on the side stream) after this rank's compute so far, i.e.
+        after every rank's prologue: peers' blocks are complete after it."""
+        self.comm.wait_stream(self.compute)
+        self._barrier_on_comm()
+
+    def fetch(self, src_rank, dst):
+        """Copies rank src_rank's K/V block into dst on the side stream;
+        returns the event the compute stream waits for before using it."""
+        import torch
+        L.copy_async(self.ctx, dst.data_ptr(), self.peers[src_rank].ptr + self.kv_offset,
+                     self.kv_bytes, self.comm)
+        ev = torch.cuda.Event()
+        ev.record(self.comm)
+        return ev
+
+    def wait(self, ev):
+        self.compute.wait_event(ev)
+
+    def release(self):
+        """Barrier after this rank's pulls: when every rank has passed it, no
+        rank reads this rank's block any more."""
+        import torch
+        self._barrier_on_comm()
+        self.released = torch.cuda.Event()
+        self.released.record(self.comm)
+
+    def close(self):
+        for m in getattr(self, "peers", []):
+            if m is not None:
+                m.close()
+        if getattr(self, "own", None) is not None:
+            self.own.close()
+            self.own = None
+
 
 @dataclass
 class RingBuffers:
@@ -112,25 +191,40 @@ class RingBuffers:
 
 
 class RingAttention:
-    """Sequence-sharded ring attention over a torch.distributed group."""
+    """Sequence-sharded attention over a torch.distributed group; the K/V
+    blocks move by `transport` ("copy" or "nccl", see the module notes)."""
 
     def __init__(self, ops, n_heads: int, head_dim: int, seq_total: int, rank: int,
-                 world: int, device, group=None, qkv_dtype=None):
+                 world: int, device, group=None, qkv_dtype=None, transport: str = "nccl"):
         import torch
         if seq_total % world:
             raise ValueError("seq_total must divide evenly over the ring")
+        if transport not in ("nccl", "copy"):
+            raise ValueError(f"unknown transport {transport!r}")
         self.ops, self.rank, self.world, self.group = ops, rank, world, group
+        self.transport = transport
         self.S = seq_total // world
         H, D, S = n_heads, head_dim, self.S
         dt = qkv_dtype or torch.float16
+        if transport == "copy":
+            qkv = ops.share((3, H, S, D), dt, device, rank, world, group)
+            nxt = ops.empty((max(world - 1, 1), 2, H, S, D), dt, device)
+        else:
+            qkv = ops.empty((3, H, S, D), dt, device)
+            nxt = ops.empty((2, H, S, D), dt, device)
         self.buf = RingBuffers(
-            qkv=ops.empty((3, H, S, D), dt, device),
-            kv_nxt=ops.empty((2, H, S, D), dt, device),
+            qkv=qkv, kv_nxt=nxt,
             o_acc=ops.empty((S, H * D), torch.float32, device),
             lse_acc=ops.empty((H, S), torch.float32, device))
 
+    def close(self) -> None:
+        if hasattr(self.ops, "close"):
+            self.ops.close()
+
     def forward(self, q, k, v, out, q_gain=None, k_gain=None, cos=None, sin=None) -> None:
         """q/k/v: this rank's token shard [1, S_loc, H, D]; out: [1, S_loc, H*D]."""
+        if self.transport == "copy":
+            return self._forward_copy(q, k, v, out, q_gain, k_gain, cos, sin)
         import torch.distributed as dist
         b = self.buf
         self.ops.prologue(q, k, v, b.qkv, q_gain, k_gain, cos, sin)
@@ -150,3 +244,21 @@ class RingAttention:
                     w.wait()
             kv_cur, kv_nxt = kv_nxt, kv_cur
         self.ops.finalize(b.o_acc, out)
+
+    def _forward_copy(self, q, k, v, out, q_gain, k_gain, cos, sin) -> None:
+        ops, b, P, r = self.ops, self.buf, self.world, self.rank
+        ops.wait_released()
+        ops.prologue(q, k, v, b.qkv, q_gain, k_gain, cos, sin)
+        events = []
+        if P > 1:
+            ops.sync_peers()
+            events = [ops.fetch((r - t) % P, b.kv_nxt[t - 1]) for t in range(1, P)]
+        qh = b.qkv[0]
+        for t in range(P):
+            kv = b.qkv[1:3] if t == 0 else b.kv_nxt[t - 1]
+            if t > 0:
+                ops.wait(events[t - 1])
+            ops.partial(qh, kv[0], kv[1], b.o_acc, b.lse_acc, merge=t > 0)
+        if P > 1:
+            ops.release()
+        ops.finalize(b.o_acc, out)

@@ -74,8 +74,32 @@ class CpuRingOps:
     def finalize(self, o_acc, out):
         out.copy_(o_acc.view(out.shape))
 
+    # "copy" transport: peers' blocks become readable after sync_peers; here
+    # an all_gather stands in for the IPC mappings
+    def share(self, shape, dtype, device, rank, world, group):
+        self.world, self.group = world, group
+        self.qkv = torch.empty(shape, dtype=torch.float64)
+        return self.qkv
 
-def _ring_worker(rank, world, port, S, H, D, q, k, v, result):
+    def wait_released(self):
+        pass
+
+    def sync_peers(self):
+        self.blocks = [torch.empty_like(self.qkv[1:3]) for _ in range(self.world)]
+        dist.all_gather(self.blocks, self.qkv[1:3].contiguous(), group=self.group)
+
+    def fetch(self, src_rank, dst):
+        dst.copy_(self.blocks[src_rank])
+        return src_rank
+
+    def wait(self, token):
+        pass
+
+    def release(self):
+        dist.barrier(group=self.group)
+
+
+def _ring_worker(rank, world, port, S, H, D, q, k, v, result, transport):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world,
@@ -84,9 +108,11 @@ def _ring_worker(rank, world, port, S, H, D, q, k, v, result):
         s_loc = S // world
         sl = slice(rank * s_loc, (rank + 1) * s_loc)
         ops = CpuRingOps(H, D, D ** -0.5)
-        ring = RingAttention(ops, H, D, S, rank, world, "cpu", qkv_dtype=torch.float64)
+        ring = RingAttention(ops, H, D, S, rank, world, "cpu", qkv_dtype=torch.float64,
+                             transport=transport)
         out = torch.empty((1, s_loc, H * D), dtype=torch.float64)
-        ring.forward(q[:, sl], k[:, sl], v[:, sl], out)
+        for _ in range(2):          # a second call reuses the buffers
+            ring.forward(q[:, sl], k[:, sl], v[:, sl], out)
         result[rank] = out[0].numpy()
     finally:
         dist.destroy_process_group()
@@ -98,14 +124,16 @@ def _free_port():
         return s.getsockname()[1]
 
 
+@pytest.mark.parametrize("transport", ["nccl", "copy"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_ring_schedule_and_merge_gloo(world):
+def test_ring_schedule_and_merge_gloo(world, transport):
     S, H, D = 48, 3, 16
     g = torch.Generator().manual_seed(world)
     q, k, v = (torch.randn((1, S, H, D), generator=g, dtype=torch.float64) for _ in range(3))
     mgr = mp.get_context("spawn").Manager()
     result = mgr.dict()
-    mp.start_processes(_ring_worker, args=(world, _free_port(), S, H, D, q, k, v, result),
+    mp.start_processes(_ring_worker, args=(world, _free_port(), S, H, D, q, k, v, result,
+                                           transport),
                        nprocs=world, join=True, start_method="spawn")
     got = np.concatenate([result[r] for r in range(world)], 0)
     s = torch.einsum("shd,thd->hst", q[0], k[0]) * D ** -0.5
