@@ -7,11 +7,14 @@
 // dependencies/zimage.c3l/shaders/flash_attn.slang:61-64, :98-101, :197-201,
 // :113-118). Rows and keys beyond seq_len are masked exactly as :120-121 do.
 //
-// CTA = 2 query tiles of 128 rows of one (b, h) = 256 queries; 320 threads:
+// CTA = 2 query tiles of 128 rows of one (b, h) = 256 queries; 384 threads:
 //   warps 0-3  softmax warpgroup for tile 0 (thread i owns query row i)
 //   warps 4-7  softmax warpgroup for tile 1
 //   warp  8    TMA producer: Q once, then K_j, V_j into an NST-slot ring
 //   warp  9    MMA issuer (one elected lane) + TMEM owner
+//   warps 10-11 idle (they complete warpgroup 2 for the register split)
+// setmaxnreg moves registers from warpgroup 2 to the softmax warpgroups,
+// which hold a whole row of 128 scores each between the two passes.
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,256+D) O1 [256+D,256+2D)
 // P_t (fp16x2) overwrites the first 64 columns of S_t after it is read.
 // MMA order per key block j (ping-pong, so one tile's softmax overlaps the
@@ -55,7 +58,14 @@ struct FaCfg {
   // then tmem base word and abort flag
   static constexpr int NBAR = 1 + 2 * NST + 2 + 4 + 1 + 1;
   static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;  // +align slack
-  static constexpr int THREADS = 320;
+  static constexpr int THREADS = 384;
+  // Register split (setmaxnreg): the two softmax warpgroups hold a whole
+  // 128-score row per thread; the producer / MMA warpgroup needs few.
+  static constexpr int REG_SOFTMAX = 216;
+  static constexpr int REG_OTHER = 64;
+  static constexpr int REG_LAUNCH = 168;  // 65536 / 384, rounded down to 8
+  static constexpr int REG_NEED = 2 * 128 * REG_SOFTMAX + 128 * REG_OTHER;
+  static_assert(REG_NEED <= THREADS * REG_LAUNCH, "register split exceeds the launch allocation");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t O_COL = 256;
 };
@@ -123,7 +133,7 @@ __device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(
 }
 
 template <int D, typename OutT>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(384, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
@@ -181,7 +191,9 @@ __global__ void __launch_bounds__(320, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
 
-  if (warp == 8) {
+  if (warp >= 8) {
+    reg_dealloc<C::REG_OTHER>();
+   if (warp == 8) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       tma_prefetch_desc(&tmQ);
@@ -219,7 +231,9 @@ __global__ void __launch_bounds__(320, 1)
     }
   } else if (warp == 9) {
     // ---------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop (so descriptors stay warp-uniform); one
+    // elected lane issues each MMA and commit.
+    {
       constexpr uint32_t IDESC_S = idesc_f16_f32(128, C::BN, 0);
       constexpr uint32_t IDESC_O = idesc_f16_f32(128, D, 1);
       const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
@@ -229,8 +243,9 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int k = 0; k < D / 16; k++) {
           const uint32_t off = (k >> 2) * C::CHUNK_BYTES + (k & 3) * 32;
-          mma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024),
-                 sdesc_sw128(ka + off, 16, 1024), IDESC_S, k > 0);
+          if (elect_one())
+            mma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024),
+                   sdesc_sw128(ka + off, 16, 1024), IDESC_S, k > 0);
         }
       };
       // O_t (+)= P_t V for the keys of one half of the block (64 keys, four
@@ -240,9 +255,10 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int kk = 0; kk < C::BN / 32; kk++) {
           const int k = half * (C::BN / 32) + kk;
-          mma_ts(tmem + C::O_COL + t * D, tmem + t * 128 + k * 8,
-                 sdesc_sw128(va + k * 2048, C::CHUNK_BYTES, 1024), IDESC_O,
-                 (acc || k > 0) ? 1u : 0u);
+          if (elect_one())
+            mma_ts(tmem + C::O_COL + t * D, tmem + t * 128 + k * 8,
+                   sdesc_sw128(va + k * 2048, C::CHUNK_BYTES, 1024), IDESC_O,
+                   (acc || k > 0) ? 1u : 0u);
         }
       };
       auto issue_o = [&](int t, int slot, bool acc, uint32_t parity) {
@@ -258,10 +274,10 @@ __global__ void __launch_bounds__(320, 1)
       if (ok) {
         tc_fence_after();
         issue_s(0, 0);
-        mma_commit(&s_full[0]);
+        if (elect_one()) mma_commit(&s_full[0]);
         issue_s(1, 0);
-        mma_commit(&s_full[1]);
-        mma_commit(&kv_empty[0]);
+        if (elect_one()) mma_commit(&s_full[1]);
+        if (elect_one()) mma_commit(&kv_empty[0]);
       }
       for (int j = 0; j < nblk && ok; j++) {
         const int uV = 2 * j + 1, sV = uV % C::NST;
@@ -273,23 +289,25 @@ __global__ void __launch_bounds__(320, 1)
           if (!mbar_wait(&kv_full[sK], (uK / C::NST) & 1, abort_flag)) break;
           tc_fence_after();
           issue_s(0, sK);
-          mma_commit(&s_full[0]);
+          if (elect_one()) mma_commit(&s_full[0]);
         }
         if (!issue_o(1, sV, j > 0, j & 1)) break;
-        mma_commit(&kv_empty[sV]);
+        if (elect_one()) mma_commit(&kv_empty[sV]);
         if (more) {
           issue_s(1, sK);
-          mma_commit(&s_full[1]);
-          mma_commit(&kv_empty[sK]);
+          if (elect_one()) mma_commit(&s_full[1]);
+          if (elect_one()) mma_commit(&kv_empty[sK]);
         }
       }
-      mma_commit(o_full);
+      if (elect_one()) mma_commit(o_full);
       // Drain: every MMA this thread issued has completed before TMEM is
       // released at the end of the kernel.
-      mma_commit(drain);
+      if (elect_one()) mma_commit(drain);
       mbar_wait_raw(drain, 0, 100000000ull);
     }
+   }
   } else {
+    reg_alloc<C::REG_SOFTMAX>();
     // ------------------------------------------------------------- softmax
     const int t = warp >> 2;                  // query tile 0 or 1
     const int row = threadIdx.x & 127;        // row within the tile = TMEM lane
@@ -315,16 +333,20 @@ __global__ void __launch_bounds__(320, 1)
       };
       // Pass 1: the row max of this block's raw scores, streaming the four
       // 32-column chunks with the next chunk's TMEM load in flight.
+      // The whole row of raw scores, loaded in one TMEM round trip and kept
+      // in registers until P is written.
+      uint32_t sbuf[128];
+#pragma unroll
+      for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, sbuf + c * 32);
+      tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 4; c++) reg_fence32(sbuf + c * 32);
+      // Pass 1: the row max of this block's raw scores.
       auto row_max = [&]() {
-        uint32_t buf[2][32];
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-        tmem_ld32(tS, buf[0]);
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          tmem_wait_ld();
-          reg_fence32(buf[c & 1]);
-          if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
-          float *v = reinterpret_cast<float *>(buf[c & 1]);
+          float *v = reinterpret_cast<float *>(sbuf + c * 32);
           mask_chunk(c, v);
 #pragma unroll
           for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = max3f(mx[(i >> 1) & 3], v[i], v[i + 1]);
@@ -332,24 +354,16 @@ __global__ void __launch_bounds__(320, 1)
         return max3f(mx[0], mx[1], fmaxf(mx[2], mx[3]));
       };
       // Pass 2: P = 2^(s*scale*log2e - m_used) as fp16 over each chunk's
-      // first 16 columns (chunk c's P lands in columns [16c, 16c+16), which
-      // belong to chunks already loaded); returns the row sum of P. No
-      // branches: every chunk is loaded (next one in flight), scaled with a
-      // packed FMA, exponentiated (a share of the pairs on the FMA pipe) and
-      // stored.
+      // first 16 columns (chunk c's P lands in columns [16c, 16c+16), whose
+      // scores are already in registers); returns the row sum of P. A share
+      // of the exponential pairs runs on the FMA pipe.
       auto emit_all = [&]() {
-        uint32_t buf[2][32];
         uint64_t part2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
         const uint64_t sl2x2 = f2_pack(sl2, sl2);
         const uint64_t neg_mx2 = f2_pack(-m_used, -m_used);
-        tmem_ld32(tS, buf[0]);
 #pragma unroll
         for (int c = 0; c < 4; c++) {
-          tmem_wait_ld();
-          reg_fence32(buf[c & 1]);
-          if (c < 3) tmem_ld32(tS + (c + 1) * 32, buf[(c + 1) & 1]);
-          float *v = reinterpret_cast<float *>(buf[c & 1]);
-          mask_chunk(c, v);
+          const float *v = reinterpret_cast<const float *>(sbuf + c * 32);
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; i++) {

@@ -120,6 +120,13 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
     CUDA_TRY(ctx, cudaFuncSetAttribute(fa_fwd_tc_kernel<D, OutT>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        C::SMEM_BYTES));
+    // setmaxnreg.inc waits until the registers it asks for are free within
+    // the block's launch allocation: never launch a split that cannot fit.
+    cudaFuncAttributes fa;
+    CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, OutT>));
+    if (fa.numRegs * C::THREADS < C::REG_NEED)
+      return fail(ctx, LLMR_ECUDA, "fa_fwd_tc: %d launch registers per thread are too few "
+                  "for the register split", fa.numRegs);
     attr_set = true;
   }
   FaParams p;

@@ -154,6 +154,10 @@ int attention(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, con
                              cudaFuncAttributeMaxDynamicSharedMemorySize,
                              C::SMEM_BYTES) != cudaSuccess)
       return LLMR_ECUDA;
+    cudaFuncAttributes fa;  // the register split must fit (see llmr_attn.cu)
+    if (cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, OutT>) != cudaSuccess ||
+        fa.numRegs * C::THREADS < C::REG_NEED)
+      return LLMR_ECUDA;
     attr_set = true;
   }
   FaParams p;

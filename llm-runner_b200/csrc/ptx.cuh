@@ -171,6 +171,15 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem,
       : "memory");
 }
 
+// One lane of the (converged) warp: true in exactly one of them.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Arrive (once) on `bar` when all previously issued tcgen05 async operations
 // of this thread have completed.
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
@@ -178,6 +187,16 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
       "[%0];" ::"r"(smem_u32(bar))
       : "memory");
+}
+
+// Warpgroup register reallocation (all four warps of a warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void reg_alloc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void reg_dealloc() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() {
