@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--transport", choices=["copy", "nccl"], default="copy",
                     help="ring mode: K/V blocks pulled from their owners on the copy engines "
                          "(copy) or passed around the ring by NCCL P2P (nccl)")
+    ap.add_argument("--cpu-table", action="store_true",
+                    help="only the CPU baseline: the oracle on all host cores and on 1 core, "
+                         "every configuration, a bounded row sample each")
     ap.add_argument("--heads", type=int, default=0,
                     help="with --profile-run: use this many heads (a smaller capture)")
     return ap.parse_args()
@@ -126,9 +129,10 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def cpu_sample(case, prep, budget_s=12.0, rows_per_chunk=512):
-    """The oracle (reference algorithm restated) on host cores over a bounded
-    row sample of one batch element. Returns (TFLOP/s, rows, seconds)."""
+def cpu_sample(case, prep, budget_s=12.0, rows_per_chunk=512, threads=0):
+    """The oracle (reference algorithm restated) on host cores (`threads`, 0 =
+    all) over a bounded row sample of one batch element. Returns (TFLOP/s,
+    rows, seconds)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     S, H, D = case.seq_len, case.n_heads, case.head_dim
@@ -138,7 +142,7 @@ def cpu_sample(case, prep, budget_s=12.0, rows_per_chunk=512):
         O.attention_block(prep.q[0], prep.k[0], prep.v[0], H, D, case.scale, eps=case.eps,
                           q_gain=prep.q_gain, k_gain=prep.k_gain,
                           split_row=min(case.split_row, S), cos=prep.cos, sin=prep.sin,
-                          exact=case.exact, rows=(0, rows))
+                          exact=case.exact, rows=(0, rows), threads=threads)
         return time.perf_counter() - t0
 
     # A short probe sizes one timed call to about `budget_s` seconds.
@@ -157,6 +161,23 @@ def config_block(case, n):
             "n_heads": case.n_heads, "seq_len": case.seq_len, "head_dim": case.head_dim,
             "parallelism": f"batch x head partition over {n} GPU(s), no collective",
             "l2": "flushed (256 MiB write) between timed steps"}
+
+
+def cpu_table(args):
+    """The oracle per configuration on all host cores and on one core, each
+    over a row sample of about 8 s, extrapolated to the whole op."""
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    cores = os.cpu_count() or 1
+    for name, case in C.CASES.items():
+        prep = C.prepare(case, L.rope_tables)
+        for threads in (0, 1):
+            tf, rows, dt = cpu_sample(case, prep, budget_s=8.0, threads=threads)
+            print(json.dumps({"cpu_table": name, "cores": cores if threads == 0 else 1,
+                              "rows_sampled": rows, "of_rows": case.seq_len, "seconds": dt,
+                              "tflops": tf, "full_op_ms_extrapolated": case.flops / (tf * 1e12) * 1e3,
+                              "kind": "port (oracle restatement of the reference shaders)"}),
+                  flush=True)
 
 
 def run_reference(args):
@@ -315,6 +336,9 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.cpu_table:
+        cpu_table(args)
         return
     if args.profile_run:
         profile_run(args)
