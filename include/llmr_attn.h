@@ -136,6 +136,12 @@ int llmr_ipc_close(llmr_ctx *ctx, void *mapped);
  * context's stream). */
 int llmr_copy_async(llmr_ctx *ctx, void *dst, const void *src, size_t bytes,
                     void *stream);
+/* cudaMemcpy2DAsync: `height` rows of `width` bytes, consecutive rows
+ * `dpitch` bytes apart in dst and `spitch` bytes apart in src (e.g. a peer's
+ * head-major K block into its slot of a buffer that keeps each head's keys
+ * from several blocks contiguous). */
+int llmr_copy2d_async(llmr_ctx *ctx, void *dst, size_t dpitch, const void *src,
+                      size_t spitch, size_t width, size_t height, void *stream);
 
 /* ---- Mirrors of the reference's attention ops (fp32 buffers) ---------- */
 
@@ -222,6 +228,11 @@ typedef struct {
   uint64_t q_row_stride, k_row_stride, v_row_stride, o_row_stride;
   uint64_t q_batch_stride, k_batch_stride, v_batch_stride, o_batch_stride;
   uint64_t q_head_stride, k_head_stride, v_head_stride;
+  /* Keys (K/V rows) per (batch, head); 0 = seq_len. A value other than
+   * seq_len needs fp16 q/k/v without LLMR_NORM_Q/NORM_K/ROPE/EXACT (no
+   * prologue): attention of seq_len queries over one block of keys, as the
+   * sequence-sharded ring computes it. Default K/V strides use it. */
+  uint32_t kv_seq_len;
 } llmr_attn_desc;
 
 /* Workspace bytes llmr_attention_fused needs for `desc`. */

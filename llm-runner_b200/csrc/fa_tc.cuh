@@ -30,8 +30,11 @@
 namespace llmr {
 
 struct FaParams {
-  int S;                 // sequence length (queries = keys)
-  int H;                 // heads; blockIdx.y = b * H + h
+  int S;                 // queries per (b, h)
+  int S_kv;              // keys per (b, h)
+  int H;                 // heads
+  int nqt;               // query-tile pairs (256 queries) per (b, h)
+  int units;             // B * H * nqt work units
   float scale_log2;      // softmax scale * log2(e)
   void *o;               // output base (OutT)
   long long o_row_stride;    // elements between consecutive tokens
@@ -53,22 +56,33 @@ struct FaCfg {
   static constexpr int Q_OFF = 0;
   static constexpr int KV_OFF = 2 * TILE_BYTES;
   static constexpr int BAR_OFF = KV_OFF + NST * TILE_BYTES;
-  // barriers: q_full, kv_full[NST], kv_empty[NST], s_full[2],
-  // p_half[2][2] (P of keys 0-63 / 64-127 of tile t written), o_full, drain;
-  // then tmem base word and abort flag
-  static constexpr int NBAR = 1 + 2 * NST + 2 + 4 + 1 + 1;
+  // barriers: q_full, q_empty, kv_full[NST], kv_empty[NST], s_full[2],
+  // p_half[2][2] (P of keys 0-63 / 64-127 of tile t written), o_full[2],
+  // o_empty[2], drain; then tmem base word and abort flag
+  static constexpr int NBAR = 2 + 2 * NST + 2 + 4 + 2 + 2 + 1;
   static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;  // +align slack
   static constexpr int THREADS = 384;
   // Register split (setmaxnreg): the two softmax warpgroups hold a whole
   // 128-score row per thread; the producer / MMA warpgroup needs few.
-  static constexpr int REG_SOFTMAX = 216;
-  static constexpr int REG_OTHER = 64;
+  static constexpr int REG_SOFTMAX = 200;
+  static constexpr int REG_OTHER = 80;
   static constexpr int REG_LAUNCH = 168;  // 65536 / 384, rounded down to 8
   static constexpr int REG_NEED = 2 * 128 * REG_SOFTMAX + 128 * REG_OTHER;
   static_assert(REG_NEED <= THREADS * REG_LAUNCH, "register split exceeds the launch allocation");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t O_COL = 256;
 };
+
+// Work decomposition of a launch: units of (b, h, 256 queries), one CTA per
+// SM walking them (the kernel keeps a whole SM: shared memory and TMEM).
+template <int D>
+inline dim3 fa_grid(FaParams &p, int B, int num_sms) {
+  using C = FaCfg<D>;
+  p.nqt = (p.S + 2 * C::BM - 1) / (2 * C::BM);
+  p.units = B * p.H * p.nqt;
+  const int sms = num_sms > 0 ? num_sms : 148;
+  return dim3(p.units < sms ? p.units : sms);
+}
 
 // Keeps every use of registers filled by tcgen05.ld after tcgen05.wait::ld.
 __device__ __forceinline__ void reg_fence32(uint32_t *r) {
@@ -149,25 +163,34 @@ __global__ void __launch_bounds__(384, 1)
   uint8_t *sKV = smem + C::KV_OFF;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
   uint64_t *q_full = bars;
-  uint64_t *kv_full = bars + 1;
-  uint64_t *kv_empty = bars + 1 + C::NST;
-  uint64_t *s_full = bars + 1 + 2 * C::NST;
+  uint64_t *q_empty = bars + 1;
+  uint64_t *kv_full = bars + 2;
+  uint64_t *kv_empty = kv_full + C::NST;
+  uint64_t *s_full = kv_empty + C::NST;
   uint64_t *p_half = s_full + 2;  // [t * 2 + half]
-  uint64_t *o_full = p_half + 4;
-  uint64_t *drain = o_full + 1;
+  uint64_t *o_full = p_half + 4;  // [t]
+  uint64_t *o_empty = o_full + 2; // [t]
+  uint64_t *drain = o_empty + 2;
   uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.S;
-  const int bh = blockIdx.y;
-  const int b = bh / p.H, h = bh % p.H;
-  const int q0 = blockIdx.x * 2 * C::BM;
-  const int nblk = (S + C::BN - 1) / C::BN;
+  const int nblk = (p.S_kv + C::BN - 1) / C::BN;  // key blocks per unit
+  // Work units (b, h, query-tile pair), persistent over the grid: this CTA
+  // takes units blockIdx.x, blockIdx.x + gridDim.x, ... Consecutive units
+  // share (b, h), so CTAs running together share K/V tiles in L2.
+  auto decode = [&](int unit, int &b, int &h, int &q0) {
+    const int bh = unit / p.nqt;
+    q0 = (unit - bh * p.nqt) * 2 * C::BM;
+    b = bh / p.H;
+    h = bh - b * p.H;
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
     for (int i = 0; i < C::NST; i++) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
@@ -176,8 +199,9 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&s_full[t], 1);
       mbar_init(&p_half[2 * t], 4);  // one arrival per softmax warp
       mbar_init(&p_half[2 * t + 1], 4);
+      mbar_init(&o_full[t], 1);
+      mbar_init(&o_empty[t], 4);
     }
-    mbar_init(o_full, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -193,47 +217,58 @@ __global__ void __launch_bounds__(384, 1)
 
   if (warp >= 8) {
     reg_dealloc<C::REG_OTHER>();
-   if (warp == 8) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
-      for (int t = 0; t < 2; t++)
-        for (int c = 0; c < C::NCHUNK; c++)
-          tma_load_4d(sQ + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, q_full,
-                      c * 64, q0 + t * C::BM, h, b);
-      bool ok = true;
-      int issued = 0;  // K/V tile loads armed so far
-      for (int j = 0; j < nblk && ok; j++) {
-        for (int kind = 0; kind < 2; kind++) {
-          const int u = 2 * j + kind;
-          const int slot = u % C::NST, round = u / C::NST;
-          if (round > 0 && !mbar_wait(&kv_empty[slot], (round - 1) & 1, abort_flag)) {
+    if (warp == 8) {
+      // ---------------------------------------------------------- producer
+      if (lane == 0) {
+        tma_prefetch_desc(&tmQ);
+        tma_prefetch_desc(&tmK);
+        tma_prefetch_desc(&tmV);
+        bool ok = true;
+        int issued = 0;  // K/V tile loads armed so far (over all units)
+        int kq = 0;      // Q loads armed so far
+        for (int unit = blockIdx.x, k = 0; unit < p.units && ok; unit += gridDim.x, k++) {
+          int b, h, q0;
+          decode(unit, b, h, q0);
+          // Q of this unit may replace the previous unit's once its last
+          // S MMAs have completed.
+          if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&kv_full[slot], C::TILE_BYTES);
-          const CUtensorMap *m = kind ? &tmV : &tmK;
-          for (int c = 0; c < C::NCHUNK; c++)
-            tma_load_4d(sKV + slot * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                        &kv_full[slot], c * 64, j * C::BN, h, b);
-          issued = u + 1;
+          mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
+          for (int t = 0; t < 2; t++)
+            for (int c = 0; c < C::NCHUNK; c++)
+              tma_load_4d(sQ + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, q_full,
+                          c * 64, q0 + t * C::BM, h, b);
+          kq = k + 1;
+          for (int j = 0; j < nblk && ok; j++) {
+            for (int kind = 0; kind < 2; kind++) {
+              const int u = 2 * (k * nblk + j) + kind;
+              const int slot = u % C::NST, round = u / C::NST;
+              if (round > 0 && !mbar_wait(&kv_empty[slot], (round - 1) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              mbar_arrive_expect_tx(&kv_full[slot], C::TILE_BYTES);
+              const CUtensorMap *m = kind ? &tmV : &tmK;
+              for (int c = 0; c < C::NCHUNK; c++)
+                tma_load_4d(sKV + slot * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
+                            &kv_full[slot], c * 64, j * C::BN, h, b);
+              issued = u + 1;
+            }
+          }
+        }
+        if (!ok) {
+          // Abort path: let every armed copy land before the CTA exits.
+          if (kq > 0) mbar_wait_raw(q_full, (kq - 1) & 1, 100000000ull);
+          for (int u = issued - C::NST < 0 ? 0 : issued - C::NST; u < issued; u++)
+            mbar_wait_raw(&kv_full[u % C::NST], (u / C::NST) & 1, 100000000ull);
         }
       }
-      if (!ok) {
-        // Abort path: let every armed copy land before the CTA exits.
-        mbar_wait_raw(q_full, 0, 100000000ull);
-        for (int u = issued - C::NST < 0 ? 0 : issued - C::NST; u < issued; u++)
-          mbar_wait_raw(&kv_full[u % C::NST], (u / C::NST) & 1, 100000000ull);
-      }
-    }
-  } else if (warp == 9) {
-    // ---------------------------------------------------------- MMA issuer
-    // The whole warp runs the loop (so descriptors stay warp-uniform); one
-    // elected lane issues each MMA and commit.
-    {
+    } else if (warp == 9) {
+      // -------------------------------------------------------- MMA issuer
+      // The whole warp runs the loop (so descriptors stay warp-uniform); one
+      // elected lane issues each MMA and commit.
       constexpr uint32_t IDESC_S = idesc_f16_f32(128, C::BN, 0);
       constexpr uint32_t IDESC_O = idesc_f16_f32(128, D, 1);
       const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
@@ -241,11 +276,11 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t qa = sQa + t * C::TILE_BYTES;
         const uint32_t ka = sKVa + slot * C::TILE_BYTES;
 #pragma unroll
-        for (int k = 0; k < D / 16; k++) {
-          const uint32_t off = (k >> 2) * C::CHUNK_BYTES + (k & 3) * 32;
+        for (int kk = 0; kk < D / 16; kk++) {
+          const uint32_t off = (kk >> 2) * C::CHUNK_BYTES + (kk & 3) * 32;
           if (elect_one())
             mma_ss(tmem + t * 128, sdesc_sw128(qa + off, 16, 1024),
-                   sdesc_sw128(ka + off, 16, 1024), IDESC_S, k > 0);
+                   sdesc_sw128(ka + off, 16, 1024), IDESC_S, kk > 0);
         }
       };
       // O_t (+)= P_t V for the keys of one half of the block (64 keys, four
@@ -254,11 +289,11 @@ __global__ void __launch_bounds__(384, 1)
         const uint32_t va = sKVa + slot * C::TILE_BYTES;
 #pragma unroll
         for (int kk = 0; kk < C::BN / 32; kk++) {
-          const int k = half * (C::BN / 32) + kk;
+          const int ks = half * (C::BN / 32) + kk;
           if (elect_one())
-            mma_ts(tmem + C::O_COL + t * D, tmem + t * 128 + k * 8,
-                   sdesc_sw128(va + k * 2048, C::CHUNK_BYTES, 1024), IDESC_O,
-                   (acc || k > 0) ? 1u : 0u);
+            mma_ts(tmem + C::O_COL + t * D, tmem + t * 128 + ks * 8,
+                   sdesc_sw128(va + ks * 2048, C::CHUNK_BYTES, 1024), IDESC_O,
+                   (acc || ks > 0) ? 1u : 0u);
         }
       };
       auto issue_o = [&](int t, int slot, bool acc, uint32_t parity) {
@@ -269,43 +304,58 @@ __global__ void __launch_bounds__(384, 1)
         }
         return true;
       };
-      bool ok = mbar_wait(q_full, 0, abort_flag);
-      if (ok) ok = mbar_wait(&kv_full[0], 0, abort_flag);
-      if (ok) {
+      bool ok = true;
+      for (int unit = blockIdx.x, k = 0; unit < p.units && ok; unit += gridDim.x, k++) {
+        const int ub = 2 * k * nblk;  // K/V ring position of this unit's K_0
+        ok = mbar_wait(q_full, k & 1, abort_flag);
+        if (ok) ok = mbar_wait(&kv_full[ub % C::NST], (ub / C::NST) & 1, abort_flag);
+        if (!ok) break;
+        // S_t of block 0 overwrites P_t of the previous unit's last block:
+        // the PV MMAs that read it were issued earlier and run first.
         tc_fence_after();
-        issue_s(0, 0);
+        issue_s(0, ub % C::NST);
         if (elect_one()) mma_commit(&s_full[0]);
-        issue_s(1, 0);
+        issue_s(1, ub % C::NST);
         if (elect_one()) mma_commit(&s_full[1]);
-        if (elect_one()) mma_commit(&kv_empty[0]);
-      }
-      for (int j = 0; j < nblk && ok; j++) {
-        const int uV = 2 * j + 1, sV = uV % C::NST;
-        const int uK = 2 * j + 2, sK = uK % C::NST;
-        const bool more = j + 1 < nblk;
-        if (!mbar_wait(&kv_full[sV], (uV / C::NST) & 1, abort_flag)) break;
-        if (!issue_o(0, sV, j > 0, j & 1)) break;
-        if (more) {
-          if (!mbar_wait(&kv_full[sK], (uK / C::NST) & 1, abort_flag)) break;
-          tc_fence_after();
-          issue_s(0, sK);
-          if (elect_one()) mma_commit(&s_full[0]);
+        if (elect_one()) mma_commit(&kv_empty[ub % C::NST]);
+        if (nblk == 1 && elect_one()) mma_commit(q_empty);
+        for (int j = 0; j < nblk; j++) {
+          const int jj = k * nblk + j;
+          const int uV = 2 * jj + 1, sV = uV % C::NST;
+          const int uK = 2 * jj + 2, sK = uK % C::NST;
+          const bool more = j + 1 < nblk;
+          if (!(ok = mbar_wait(&kv_full[sV], (uV / C::NST) & 1, abort_flag))) break;
+          // O_t is overwritten by this unit's first PV: the previous unit's
+          // epilogue must have read it.
+          if (j == 0 && k > 0 && !(ok = mbar_wait(&o_empty[0], (k - 1) & 1, abort_flag))) break;
+          if (!(ok = issue_o(0, sV, j > 0, jj & 1))) break;
+          if (more) {
+            if (!(ok = mbar_wait(&kv_full[sK], (uK / C::NST) & 1, abort_flag))) break;
+            tc_fence_after();
+            issue_s(0, sK);
+            if (elect_one()) mma_commit(&s_full[0]);
+          } else {
+            if (elect_one()) mma_commit(&o_full[0]);
+          }
+          if (j == 0 && k > 0 && !(ok = mbar_wait(&o_empty[1], (k - 1) & 1, abort_flag))) break;
+          if (!(ok = issue_o(1, sV, j > 0, jj & 1))) break;
+          if (elect_one()) mma_commit(&kv_empty[sV]);
+          if (more) {
+            issue_s(1, sK);
+            if (elect_one()) mma_commit(&s_full[1]);
+            if (elect_one()) mma_commit(&kv_empty[sK]);
+            // The unit's last S MMAs are issued: Q may be replaced after them.
+            if (j + 2 == nblk && elect_one()) mma_commit(q_empty);
+          } else {
+            if (elect_one()) mma_commit(&o_full[1]);
+          }
         }
-        if (!issue_o(1, sV, j > 0, j & 1)) break;
-        if (elect_one()) mma_commit(&kv_empty[sV]);
-        if (more) {
-          issue_s(1, sK);
-          if (elect_one()) mma_commit(&s_full[1]);
-          if (elect_one()) mma_commit(&kv_empty[sK]);
-        }
       }
-      if (elect_one()) mma_commit(o_full);
-      // Drain: every MMA this thread issued has completed before TMEM is
+      // Drain: every MMA this warp issued has completed before TMEM is
       // released at the end of the kernel.
       if (elect_one()) mma_commit(drain);
       mbar_wait_raw(drain, 0, 100000000ull);
     }
-   }
   } else {
     reg_alloc<C::REG_SOFTMAX>();
     // ------------------------------------------------------------- softmax
@@ -315,34 +365,36 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tS = tmem + lane_off + t * 128;
     const uint32_t tO = tmem + lane_off + C::O_COL + t * D;
     const float sl2 = p.scale_log2;
-    float m_used = -INFINITY;  // log2-domain max the P values are relative to
-    float l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < nblk; j++) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], j & 1, abort_flag));
-      if (!ok) break;
-      tc_fence_after();
-      const int valid = S - j * C::BN;  // keys of this block below seq_len
-      // Applies the key mask (keys >= seq_len -> -inf) to chunk c.
-      auto mask_chunk = [&](int c, float *v) {
-        if (valid < C::BN) {
+    for (int unit = blockIdx.x, k = 0; unit < p.units && ok; unit += gridDim.x, k++) {
+      int b, h, q0;
+      decode(unit, b, h, q0);
+      const int bh = b * p.H + h;
+      float m_used = -INFINITY;  // log2-domain max the P values are relative to
+      float l = 0.0f;
+      for (int j = 0; j < nblk; j++) {
+        const int jj = k * nblk + j;
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], jj & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const int valid = p.S_kv - j * C::BN;  // keys of this block below S_kv
+        // Applies the key mask (keys >= S_kv -> -inf) to chunk c.
+        auto mask_chunk = [&](int c, float *v) {
+          if (valid < C::BN) {
 #pragma unroll
-          for (int i = 0; i < 32; i++)
-            if (c * 32 + i >= valid) v[i] = -INFINITY;
-        }
-      };
-      // Pass 1: the row max of this block's raw scores, streaming the four
-      // 32-column chunks with the next chunk's TMEM load in flight.
-      // The whole row of raw scores, loaded in one TMEM round trip and kept
-      // in registers until P is written.
-      uint32_t sbuf[128];
+            for (int i = 0; i < 32; i++)
+              if (c * 32 + i >= valid) v[i] = -INFINITY;
+          }
+        };
+        // The whole row of raw scores, loaded in one TMEM round trip and kept
+        // in registers until P is written.
+        uint32_t sbuf[128];
 #pragma unroll
-      for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, sbuf + c * 32);
-      tmem_wait_ld();
+        for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, sbuf + c * 32);
+        tmem_wait_ld();
 #pragma unroll
-      for (int c = 0; c < 4; c++) reg_fence32(sbuf + c * 32);
-      // Pass 1: the row max of this block's raw scores.
-      auto row_max = [&]() {
+        for (int c = 0; c < 4; c++) reg_fence32(sbuf + c * 32);
+        // Pass 1: the row max of this block's raw scores.
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
         for (int c = 0; c < 4; c++) {
@@ -351,13 +403,34 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = max3f(mx[(i >> 1) & 3], v[i], v[i + 1]);
         }
-        return max3f(mx[0], mx[1], fmaxf(mx[2], mx[3]));
-      };
-      // Pass 2: P = 2^(s*scale*log2e - m_used) as fp16 over each chunk's
-      // first 16 columns (chunk c's P lands in columns [16c, 16c+16), whose
-      // scores are already in registers); returns the row sum of P. A share
-      // of the exponential pairs runs on the FMA pipe.
-      auto emit_all = [&]() {
+        // Lazy max: the max the P values are relative to moves only when this
+        // block's row max passes it by more than kMaxExp (P would overflow
+        // fp16), and on the first block; O and l are rescaled then.
+        const float m_new = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sl2;
+        const bool need = m_new > m_used + kMaxExp;  // always true on block 0
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_tgt = need ? m_new : m_used;
+          const float factor = ex2_approx(m_used - m_tgt);  // 0 on the first block
+          l *= factor;
+          if (j > 0) {
+#pragma unroll 1
+            for (int c = 0; c < D / 32; c++) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_wait_ld();
+              reg_fence32(o);
+#pragma unroll
+              for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+              tmem_st32(tO + c * 32, o);
+            }
+          }
+          m_used = m_tgt;
+        }
+        // Pass 2: P = 2^(s*scale*log2e - m_used) as fp16 over each chunk's
+        // first 16 columns (chunk c's P lands in columns [16c, 16c+16), whose
+        // scores are already in registers). A share of the exponential pairs
+        // runs on the FMA pipe. Each half of P (keys 0-63, then 64-127) is
+        // handed to the MMA warp as soon as it is in TMEM.
         uint64_t part2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
         const uint64_t sl2x2 = f2_pack(sl2, sl2);
         const uint64_t neg_mx2 = f2_pack(-m_used, -m_used);
@@ -379,8 +452,6 @@ __global__ void __launch_bounds__(384, 1)
           }
           tmem_st16(tS + c * 16, pk);
           if (c == 1 || c == 3) {
-            // Half of P (keys 0-63, then 64-127) is in TMEM: let the MMA
-            // warp start that half of O += P V while the rest is computed.
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
@@ -388,35 +459,12 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
-        return (s0.x + s0.y) + (s1.x + s1.y);
-      };
-      // Lazy max: the max the P values are relative to moves only when this
-      // block's row max passes it by more than kMaxExp (P would overflow
-      // fp16), and on the first block; O and l are rescaled then.
-      const float m_new = row_max() * sl2;
-      const bool need = m_new > m_used + kMaxExp;  // always true on block 0
-      if (__any_sync(0xffffffffu, need)) {
-        const float m_tgt = need ? m_new : m_used;
-        const float factor = ex2_approx(m_used - m_tgt);  // 0 on the first block
-        l *= factor;
-        if (j > 0) {
-#pragma unroll 1
-          for (int c = 0; c < D / 32; c++) {
-            uint32_t o[32];
-            tmem_ld32(tO + c * 32, o);
-            tmem_wait_ld();
-            reg_fence32(o);
-#pragma unroll
-            for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-            tmem_st32(tO + c * 32, o);
-          }
-        }
-        m_used = m_tgt;
+        l += (s0.x + s0.y) + (s1.x + s1.y);
       }
-      l += emit_all();
-    }
-    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, abort_flag));
-    if (ok) {
+      if (!ok) break;
+      // ------------------------------------------------------- epilogue
+      ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], k & 1, abort_flag));
+      if (!ok) break;
       tc_fence_after();
       const int qrow = q0 + t * C::BM + row;
       OutT *dst = reinterpret_cast<OutT *>(p.o) + (long long)b * p.o_batch_stride +
@@ -430,12 +478,12 @@ __global__ void __launch_bounds__(384, 1)
       const bool merge = kCanMerge && p.merge && qrow < S;
       if (merge) {
         const float la = p.lse[(long long)bh * S + qrow];
-        const float mx = fmaxf(la, lse_t);
-        const float wa = expf(la - mx), wt = expf(lse_t - mx);
+        const float mx2 = fmaxf(la, lse_t);
+        const float wa = expf(la - mx2), wt = expf(lse_t - mx2);
         const float inv = 1.0f / (wa + wt);
         ca = wa * inv;
         ct = wt * inv / l;
-        lse_out = mx + logf(wa + wt);
+        lse_out = mx2 + logf(wa + wt);
       }
 #pragma unroll
       for (int c = 0; c < D / 32; c++) {
@@ -443,6 +491,12 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
         reg_fence32(o);
+        if (c == D / 32 - 1) {
+          // O_t is read out: the next unit's first PV may overwrite it.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&o_empty[t]);
+        }
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[i]) * ct;

@@ -112,7 +112,7 @@ int make_map(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S,
 
 template <int D, typename OutT>
 int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
-                 const CUtensorMap &mv, int B, int H, int S, float scale, void *o,
+                 const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
                  long long o_rs, long long o_bs, float *lse, int merge) {
   using C = FaCfg<D>;
   static bool attr_set = false;
@@ -131,6 +131,7 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   }
   FaParams p;
   p.S = S;
+  p.S_kv = S_kv;
   p.H = H;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.o = o;
@@ -139,23 +140,29 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   p.lse = lse;
   p.merge = merge;
   p.err = ctx->d_err;
-  dim3 grid((S + 2 * C::BM - 1) / (2 * C::BM), B * H);
+  const dim3 grid = fa_grid<D>(p, B, ctx->num_sms);
   fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
   return after_launch(ctx, "fa_fwd_tc");
 }
 
 int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
-                     const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S,
+                     const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S, int S_kv,
                      float scale, void *o, long long o_rs, long long o_bs, float *lse,
                      int merge) {
   if (D == 128) {
-    if (od == LLMR_F32) return launch_fa_tc<128, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, merge);
-    if (od == LLMR_F16) return launch_fa_tc<128, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
-    return launch_fa_tc<128, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
+    if (od == LLMR_F32)
+      return launch_fa_tc<128, float>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, merge);
+    if (od == LLMR_F16)
+      return launch_fa_tc<128, __half>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, 0);
+    return launch_fa_tc<128, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs,
+                                            lse, 0);
   }
-  if (od == LLMR_F32) return launch_fa_tc<64, float>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, merge);
-  if (od == LLMR_F16) return launch_fa_tc<64, __half>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
-  return launch_fa_tc<64, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, 0);
+  if (od == LLMR_F32)
+    return launch_fa_tc<64, float>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, merge);
+  if (od == LLMR_F16)
+    return launch_fa_tc<64, __half>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, 0);
+  return launch_fa_tc<64, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse,
+                                         0);
 }
 
 template <int D, typename InT, typename OutT>
@@ -233,8 +240,8 @@ int check_ctx(llmr_ctx *ctx) {
 
 // Fills default strides for a desc (elements). Order: {batch, row, head}.
 void default_strides(const llmr_attn_desc *d, uint64_t rs_in, uint64_t bs_in, uint64_t hs_in,
-                     long long *out) {
-  const long long H = d->n_heads, S = d->seq_len, D = d->head_dim;
+                     long long *out, long long rows) {
+  const long long H = d->n_heads, S = rows, D = d->head_dim;
   long long rs, hs, bs;
   if (d->layout == LLMR_LAYOUT_BSHD) {
     rs = H * D;
@@ -427,6 +434,18 @@ int llmr_copy_async(llmr_ctx *ctx, void *dst, const void *src, size_t bytes, voi
   return LLMR_OK;
 }
 
+int llmr_copy2d_async(llmr_ctx *ctx, void *dst, size_t dpitch, const void *src, size_t spitch,
+                      size_t width, size_t height, void *stream) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (width == 0 || height == 0) return LLMR_OK;
+  if (!dst || !src || width > dpitch || width > spitch)
+    return fail(ctx, LLMR_EINVAL, "bad 2-D copy geometry");
+  cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
+  CUDA_TRY(ctx, cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDefault, s));
+  return LLMR_OK;
+}
+
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {
   if (!d) return 0;
   const size_t n = (size_t)d->batch * d->n_heads * d->seq_len * d->head_dim;
@@ -459,11 +478,15 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
   const size_t need = llmr_attention_workspace_bytes(d);
   if (need > ctx->ws_bytes)
     return fail(ctx, LLMR_ENOMEM, "workspace %zu bytes < %zu needed (llmr_ctx_reserve)", ctx->ws_bytes, need);
+  const int S_kv = d->kv_seq_len ? (int)d->kv_seq_len : S;
+  if (S_kv != S && need != 0)
+    return fail(ctx, LLMR_EINVAL, "kv_seq_len != seq_len needs fp16 q/k/v without norm, RoPE or "
+                                  "LLMR_EXACT");
 
   long long qs[3], ks[3], vs[3];
-  default_strides(d, d->q_row_stride, d->q_batch_stride, d->q_head_stride, qs);
-  default_strides(d, d->k_row_stride, d->k_batch_stride, d->k_head_stride, ks);
-  default_strides(d, d->v_row_stride, d->v_batch_stride, d->v_head_stride, vs);
+  default_strides(d, d->q_row_stride, d->q_batch_stride, d->q_head_stride, qs, S);
+  default_strides(d, d->k_row_stride, d->k_batch_stride, d->k_head_stride, ks, S_kv);
+  default_strides(d, d->v_row_stride, d->v_batch_stride, d->v_head_stride, vs, S_kv);
   const long long o_rs = d->o_row_stride ? (long long)d->o_row_stride : (long long)H * D;
   const long long o_bs = d->o_batch_stride ? (long long)d->o_batch_stride : (long long)S * o_rs;
   float *lse_out = (d->flags & LLMR_LSE) ? lse : nullptr;
@@ -515,8 +538,8 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
   const bool direct = need == 0;
   if (direct) {
     if ((rc = make_map(ctx, &mq, q, D, S, H, B, qs[1], qs[2], qs[0]))) return rc;
-    if ((rc = make_map(ctx, &mk, k, D, S, H, B, ks[1], ks[2], ks[0]))) return rc;
-    if ((rc = make_map(ctx, &mv, v, D, S, H, B, vs[1], vs[2], vs[0]))) return rc;
+    if ((rc = make_map(ctx, &mk, k, D, S_kv, H, B, ks[1], ks[2], ks[0]))) return rc;
+    if ((rc = make_map(ctx, &mv, v, D, S_kv, H, B, vs[1], vs[2], vs[0]))) return rc;
   } else {
     __half *w = static_cast<__half *>(ctx->ws);
     rc = launch_prologue<__half>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
@@ -528,8 +551,8 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
     if ((rc = make_map(ctx, &mv, w + 2 * plane, D, S, H, B, rs, hs, bs))) return rc;
   }
   mark(1);
-  rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o, o_rs, o_bs,
-                        lse_out, (d->flags & LLMR_MERGE) ? 1 : 0);
+  rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
+                        o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0);
   mark(2);
   ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
   return rc;
@@ -578,9 +601,9 @@ int llmr_attention_prologue(llmr_ctx *ctx, const llmr_attn_desc *d, const void *
   if (reinterpret_cast<uintptr_t>(qkv_out) & 15)
     return fail(ctx, LLMR_EINVAL, "qkv_out must be 16-byte aligned");
   long long qs[3], ks[3], vs[3];
-  default_strides(d, d->q_row_stride, d->q_batch_stride, d->q_head_stride, qs);
-  default_strides(d, d->k_row_stride, d->k_batch_stride, d->k_head_stride, ks);
-  default_strides(d, d->v_row_stride, d->v_batch_stride, d->v_head_stride, vs);
+  default_strides(d, d->q_row_stride, d->q_batch_stride, d->q_head_stride, qs, d->seq_len);
+  default_strides(d, d->k_row_stride, d->k_batch_stride, d->k_head_stride, ks, d->seq_len);
+  default_strides(d, d->v_row_stride, d->v_batch_stride, d->v_head_stride, vs, d->seq_len);
   ProParams pp;
   pp.B = B;
   pp.S = S;

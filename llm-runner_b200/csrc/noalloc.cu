@@ -144,9 +144,9 @@ int prologue(cudaStream_t st, int num_sms, const void *q, const void *k, const v
 }
 
 template <int D, typename OutT>
-int attention(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, const CUtensorMap &mv,
-              int B, int H, int S, float scale, void *o, long long o_rs, long long o_bs,
-              float *lse, int *err) {
+int attention(cudaStream_t st, int num_sms, const CUtensorMap &mq, const CUtensorMap &mk,
+              const CUtensorMap &mv, int B, int H, int S, float scale, void *o, long long o_rs,
+              long long o_bs, float *lse, int *err) {
   using C = FaCfg<D>;
   static bool attr_set = false;  // per-process, like a kernel attribute
   if (!attr_set) {
@@ -162,6 +162,7 @@ int attention(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, con
   }
   FaParams p;
   p.S = S;
+  p.S_kv = S;
   p.H = H;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.o = o;
@@ -170,18 +171,21 @@ int attention(cudaStream_t st, const CUtensorMap &mq, const CUtensorMap &mk, con
   p.lse = lse;
   p.merge = 0;
   p.err = err;
-  dim3 grid((S + 2 * C::BM - 1) / (2 * C::BM), B * H);
+  const dim3 grid = fa_grid<D>(p, B, num_sms);
   fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(mq, mk, mv, p);
   return cudaGetLastError() == cudaSuccess ? LLMR_OK : LLMR_ECUDA;
 }
 
 template <int D>
-int attention_any(cudaStream_t st, llmr_dtype od, const CUtensorMap &mq, const CUtensorMap &mk,
-                  const CUtensorMap &mv, int B, int H, int S, float scale, void *o,
-                  long long o_rs, long long o_bs, float *lse, int *err) {
-  if (od == LLMR_F32) return attention<D, float>(st, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, err);
-  if (od == LLMR_F16) return attention<D, __half>(st, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, err);
-  return attention<D, __nv_bfloat16>(st, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, err);
+int attention_any(cudaStream_t st, int num_sms, llmr_dtype od, const CUtensorMap &mq,
+                  const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S, float scale,
+                  void *o, long long o_rs, long long o_bs, float *lse, int *err) {
+  if (od == LLMR_F32)
+    return attention<D, float>(st, num_sms, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, err);
+  if (od == LLMR_F16)
+    return attention<D, __half>(st, num_sms, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse, err);
+  return attention<D, __nv_bfloat16>(st, num_sms, mq, mk, mv, B, H, S, scale, o, o_rs, o_bs, lse,
+                                     err);
 }
 
 void strides_for(const llmr_attn_desc *d, uint64_t rs_in, uint64_t bs_in, uint64_t hs_in,
@@ -207,6 +211,7 @@ extern "C" int llmr_attention_fused_noalloc(const llmr_attn_desc *d, const void 
   if (d->in_dtype > LLMR_BF16 || d->out_dtype > LLMR_BF16 || d->layout > LLMR_LAYOUT_BHSD)
     return LLMR_EINVAL;
   if (d->flags & (LLMR_EXACT | LLMR_MERGE)) return LLMR_EINVAL;  // plain tensor-core path only
+  if (d->kv_seq_len != 0 && d->kv_seq_len != d->seq_len) return LLMR_EINVAL;
   if (((d->flags & LLMR_NORM_Q) && !q_gain) || ((d->flags & LLMR_NORM_K) && !k_gain) ||
       ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) || ((d->flags & LLMR_LSE) && !lse))
     return LLMR_EINVAL;
@@ -268,8 +273,8 @@ extern "C" int llmr_attention_fused_noalloc(const llmr_attn_desc *d, const void 
   }
   float *lse_out = (d->flags & LLMR_LSE) ? lse : nullptr;
   if (D == 128)
-    return attention_any<128>(st, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o, o_rs, o_bs,
-                              lse_out, dev->err);
-  return attention_any<64>(st, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o, o_rs, o_bs,
-                           lse_out, dev->err);
+    return attention_any<128>(st, dev->num_sms, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o,
+                              o_rs, o_bs, lse_out, dev->err);
+  return attention_any<64>(st, dev->num_sms, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o,
+                           o_rs, o_bs, lse_out, dev->err);
 }

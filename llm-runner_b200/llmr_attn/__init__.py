@@ -66,6 +66,7 @@ class AttnDesc(ctypes.Structure):
         ("v_batch_stride", ctypes.c_uint64), ("o_batch_stride", ctypes.c_uint64),
         ("q_head_stride", ctypes.c_uint64), ("k_head_stride", ctypes.c_uint64),
         ("v_head_stride", ctypes.c_uint64),
+        ("kv_seq_len", ctypes.c_uint32),
     ]
 
 
@@ -119,6 +120,8 @@ def _load() -> ctypes.CDLL:
         "llmr_ipc_open": (i32, [vp, ctypes.POINTER(IpcHandle), ctypes.POINTER(vp)]),
         "llmr_ipc_close": (i32, [vp, vp]),
         "llmr_copy_async": (i32, [vp, vp, vp, ctypes.c_size_t, vp]),
+        "llmr_copy2d_async": (i32, [vp, vp, ctypes.c_size_t, vp, ctypes.c_size_t,
+                                    ctypes.c_size_t, ctypes.c_size_t, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -286,9 +289,10 @@ class AttnConfig:
 
 def make_desc(cfg: AttnConfig, batch: int, seq_len: int, in_dtype: int, out_dtype: int,
               lse: bool = False, strides: Optional[dict] = None,
-              merge: bool = False) -> AttnDesc:
+              merge: bool = False, kv_len: int = 0) -> AttnDesc:
     d = AttnDesc()
     d.batch, d.n_heads, d.seq_len, d.head_dim = batch, cfg.n_heads, seq_len, cfg.head_dim
+    d.kv_seq_len = kv_len
     d.in_dtype, d.out_dtype, d.layout = in_dtype, out_dtype, cfg.layout
     d.flags = ((NORM_Q if cfg.norm_q else 0) | (NORM_K if cfg.norm_k else 0)
                | (ROPE if cfg.rope else 0) | (EXACT if cfg.exact else 0)
@@ -306,16 +310,18 @@ def workspace_bytes(desc: AttnDesc) -> int:
 
 def attention_fused(ctx: Context, q, k, v, o, cfg: AttnConfig, *, batch: int, seq_len: int,
                     q_gain=None, k_gain=None, cos=None, sin=None, lse=None,
-                    strides: Optional[dict] = None, merge: bool = False) -> None:
+                    strides: Optional[dict] = None, merge: bool = False,
+                    kv_len: int = 0) -> None:
     """Fused QK-RMSNorm + RoPE + non-causal attention into `o` [B,S,H*D].
 
     q/k/v: torch CUDA tensors (f32/f16/bf16) in cfg.layout; gains fp32
     [D] or [2,D] (txt/img split at cfg.split_row); cos/sin fp32 [rows, D/2].
     merge: o (fp32) and lse already hold a result over other keys; this
     call's result is merged into them by log-sum-exp.
+    kv_len: keys per (b, h) when not seq_len (fp16 q/k/v without norm/RoPE).
     """
     desc = make_desc(cfg, batch, seq_len, _dtype_code(q), _dtype_code(o),
-                     lse=lse is not None, strides=strides, merge=merge)
+                     lse=lse is not None, strides=strides, merge=merge, kv_len=kv_len)
     ctx.check(lib.llmr_attention_fused(ctx.handle, ctypes.byref(desc), _ptr(q), _ptr(k),
                                        _ptr(v), _ptr(q_gain), _ptr(k_gain), _ptr(cos),
                                        _ptr(sin), _ptr(o), _ptr(lse)))
@@ -437,6 +443,17 @@ def copy_async(ctx: Context, dst: int, src: int, nbytes: int, stream=None) -> No
                                   nbytes, ctypes.c_void_p(raw or None)))
 
 
+def copy2d_async(ctx: Context, dst: int, dpitch: int, src: int, spitch: int, width: int,
+                 height: int, stream=None) -> None:
+    """`height` rows of `width` bytes between strided row sets (copy engines)."""
+    raw = None
+    if stream is not None:
+        raw = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+    ctx.check(lib.llmr_copy2d_async(ctx.handle, ctypes.c_void_p(dst), dpitch,
+                                    ctypes.c_void_p(src), spitch, width, height,
+                                    ctypes.c_void_p(raw or None)))
+
+
 # ------------------------------------------------------------------- host helpers
 
 def rope_tables(pos: np.ndarray, axes_dims: Sequence[int], theta: float):
@@ -463,6 +480,6 @@ __all__ = [
     "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
     "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
     "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
-    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "IpcHandle", "LIB_PATH",
+    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "IpcHandle", "LIB_PATH",
     "lib",
 ]

@@ -20,8 +20,10 @@ Two schemes, both new relative to the reference (which is single-GPU,
     blocks straight from their owners on the copy engines, in step order,
     on a side stream, while the attention kernel runs on all SMs. NVSwitch
     gives every pair full bandwidth, so no block is passed on hop by hop.
-    A second barrier after the pulls lets owners overwrite their block in
-    the next call.
+    Received blocks are stored so that each head's keys of all blocks are
+    contiguous, and the kernel covers groups of arrived blocks in one launch
+    (`ring_groups`: own block, then 2, 4, ... blocks). A second barrier
+    after the pulls lets owners overwrite their block in the next call.
   - "nccl": the classic ring: the current block goes to rank r+1 and the
     next one comes from rank r-1 by NCCL P2P (batch_isend_irecv) each step.
 
@@ -100,11 +102,14 @@ class RingOps:
                              q_gain=q_gain, k_gain=k_gain, cos=cos, sin=sin)
 
     def partial(self, qh, kh, vh, o, lse, merge):
-        """Attention of this rank's Q against one K/V block into (o, lse);
-        with merge, folded into the result already there (log-sum-exp merge
-        in the kernel's epilogue)."""
+        """Attention of this rank's Q [H, S, D] against the keys of kh / vh
+        ([H, T, D] views, T a multiple of the shard length, any head stride)
+        into (o, lse); with merge, folded into the result already there
+        (log-sum-exp merge in the kernel's epilogue)."""
+        st = {"k_row_stride": kh.stride(1), "k_head_stride": kh.stride(0),
+              "v_row_stride": vh.stride(1), "v_head_stride": vh.stride(0)}
         L.attention_fused(self.ctx, qh, kh, vh, o, self.part_cfg, batch=1, seq_len=self.S,
-                          lse=lse, merge=merge)
+                          lse=lse, merge=merge, kv_len=kh.shape[1], strides=st)
 
     def finalize(self, o_acc, out):
         L.convert_f32(self.ctx, o_acc, out)
@@ -152,12 +157,20 @@ class RingOps:
         self.comm.wait_stream(self.compute)
         self._barrier_on_comm()
 
-    def fetch(self, src_rank, dst):
-        """Copies rank src_rank's K/V block into dst on the side stream;
-        returns the event the compute stream waits for before using it."""
+    def fetch(self, src_rank, slot, kv_recv):
+        """Copies rank src_rank's K/V block ([2][H][S][D]) into slot `slot` of
+        kv_recv ([2][H][n_slots*S][D], each head's keys of all slots
+        contiguous) on the side stream, one 2-D copy per K and V; returns the
+        event the compute stream waits for before using it."""
         import torch
-        L.copy_async(self.ctx, dst.data_ptr(), self.peers[src_rank].ptr + self.kv_offset,
-                     self.kv_bytes, self.comm)
+        _, H, T, D = kv_recv.shape
+        S = self.S
+        esize = kv_recv.element_size()
+        row = S * D * esize                       # one head of one block
+        for i in range(2):
+            dst = kv_recv[i].data_ptr() + slot * row
+            src = self.peers[src_rank].ptr + self.kv_offset + i * H * row
+            L.copy2d_async(self.ctx, dst, T * D * esize, src, row, row, H, self.comm)
         ev = torch.cuda.Event()
         ev.record(self.comm)
         return ev
@@ -208,7 +221,7 @@ class RingAttention:
         dt = qkv_dtype or torch.float16
         if transport == "copy":
             qkv = ops.share((3, H, S, D), dt, device, rank, world, group)
-            nxt = ops.empty((max(world - 1, 1), 2, H, S, D), dt, device)
+            nxt = ops.empty((2, H, max(world - 1, 1) * S, D), dt, device)
         else:
             qkv = ops.empty((3, H, S, D), dt, device)
             nxt = ops.empty((2, H, S, D), dt, device)
@@ -246,19 +259,36 @@ class RingAttention:
         self.ops.finalize(b.o_acc, out)
 
     def _forward_copy(self, q, k, v, out, q_gain, k_gain, cos, sin) -> None:
-        ops, b, P, r = self.ops, self.buf, self.world, self.rank
+        ops, b, P, r, S = self.ops, self.buf, self.world, self.rank, self.S
         ops.wait_released()
         ops.prologue(q, k, v, b.qkv, q_gain, k_gain, cos, sin)
         events = []
         if P > 1:
             ops.sync_peers()
-            events = [ops.fetch((r - t) % P, b.kv_nxt[t - 1]) for t in range(1, P)]
+            # slot t-1 receives the block of rank (r - t) mod P, in step order
+            events = [ops.fetch((r - t) % P, t - 1, b.kv_nxt) for t in range(1, P)]
         qh = b.qkv[0]
-        for t in range(P):
-            kv = b.qkv[1:3] if t == 0 else b.kv_nxt[t - 1]
-            if t > 0:
-                ops.wait(events[t - 1])
-            ops.partial(qh, kv[0], kv[1], b.o_acc, b.lse_acc, merge=t > 0)
+        ops.partial(qh, b.qkv[1], b.qkv[2], b.o_acc, b.lse_acc, merge=False)
+        for a, n in ring_groups(P - 1):
+            ops.wait(events[a + n - 1])   # copies run in order on one stream
+            ops.partial(qh, b.kv_nxt[0][:, a * S:(a + n) * S], b.kv_nxt[1][:, a * S:(a + n) * S],
+                        b.o_acc, b.lse_acc, merge=True)
         if P > 1:
             ops.release()
         ops.finalize(b.o_acc, out)
+
+
+def ring_groups(n: int) -> List[Tuple[int, int]]:
+    """Received blocks 0..n-1 as consecutive (first, count) groups of
+    doubling size (2, 4, 8, ...), the last group taking the remainder: one
+    attention launch per group, each starting while the later blocks are
+    still being copied. n=7 -> [(0, 2), (2, 5)]."""
+    groups, i, size = [], 0, 2
+    while i < n:
+        take = min(size, n - i)
+        if n - (i + take) < 2 * size:
+            take = n - i
+        groups.append((i, take))
+        i += take
+        size *= 2
+    return groups

@@ -13,7 +13,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from llmr_attn.dist import RingAttention, partition_units
+from llmr_attn.dist import RingAttention, partition_units, ring_groups
 
 
 @pytest.mark.parametrize("B,H,world", [(1, 24, 1), (1, 24, 8), (2, 30, 8), (1, 24, 7),
@@ -31,6 +31,22 @@ def test_partition_units_cover_and_balance(B, H, world):
         sizes.append(n)
     assert sorted(seen) == list(range(B * H))
     assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("n", range(0, 20))
+def test_ring_groups_cover_in_order(n):
+    groups = ring_groups(n)
+    covered = [i for a, c in groups for i in range(a, a + c)]
+    assert covered == list(range(n))
+    assert all(c >= 1 for _, c in groups)
+    if n >= 2:
+        assert groups[0] == (0, min(2, n)) or len(groups) == 1
+
+
+def test_ring_groups_eight_gpus():
+    assert ring_groups(7) == [(0, 2), (2, 5)]
+    assert ring_groups(1) == [(0, 1)]
+    assert ring_groups(3) == [(0, 3)]
 
 
 def test_partition_zimage_8_gpus():
@@ -53,6 +69,7 @@ class CpuRingOps:
             qkv_out[i] = t[0].permute(1, 0, 2).to(torch.float64)
 
     def partial(self, qh, kh, vh, o, lse, merge):
+        assert kh.shape[1] % qh.shape[1] == 0   # whole blocks of keys
         s = torch.einsum("hsd,htd->hst", qh, kh) * self.scale
         m = s.amax(-1, keepdim=True)
         p = torch.exp(s - m)
@@ -88,8 +105,9 @@ class CpuRingOps:
         self.blocks = [torch.empty_like(self.qkv[1:3]) for _ in range(self.world)]
         dist.all_gather(self.blocks, self.qkv[1:3].contiguous(), group=self.group)
 
-    def fetch(self, src_rank, dst):
-        dst.copy_(self.blocks[src_rank])
+    def fetch(self, src_rank, slot, kv_recv):
+        S = self.blocks[src_rank].shape[2]
+        kv_recv[:, :, slot * S:(slot + 1) * S].copy_(self.blocks[src_rank])
         return src_rank
 
     def wait(self, token):

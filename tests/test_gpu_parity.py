@@ -158,6 +158,25 @@ def test_tc_kernel_ragged_shapes(ctx, D, S):
 
 
 @pytest.mark.parametrize("D", [64, 128])
+def test_tc_kernel_many_units_per_cta(ctx, D):
+    """More (b, h, 256-query) units than SMs: the persistent kernel walks
+    several units per CTA (TMEM, barriers and the K/V ring carry over), with
+    a ragged last tile and a ragged last key block in every unit."""
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(300 + D)
+    B, S, H = 3, 257, 52          # 3 * 52 * 2 = 312 units
+    q, k, v = (rng.standard_normal((B, S, H, D), dtype=np.float32) for _ in range(3))
+    q, k, v = (a.astype(np.float16).astype(np.float32) for a in (q, k, v))
+    scale = D ** -0.5
+    o = torch.empty((B, S, H * D), device="cuda", dtype=torch.float32)
+    L.attention_fused(ctx, dev(q).half(), dev(k).half(), dev(v).half(), o,
+                      L.AttnConfig(n_heads=H, head_dim=D, scale=scale), batch=B, seq_len=S)
+    ctx.sync()
+    check(host(o), oracle_fa(q, k, v, scale).reshape(B, S, H * D), what=f"units D={D}")
+
+
+@pytest.mark.parametrize("D", [64, 128])
 def test_tc_kernel_rescale_paths(ctx, D):
     """Scores that jump inside later key blocks, at different 32-key chunk
     positions: some jumps stay below the lazy-rescale threshold (P up to
@@ -327,6 +346,49 @@ def test_merge_flag_combines_key_blocks(ctx, D):
     assert ei.value.status == L.EINVAL
     with pytest.raises(L.LlmrError) as ei:
         L.attention_fused(ctx, qh, kh, kh, o, cfg, batch=1, seq_len=S, merge=True)
+    assert ei.value.status == L.EINVAL
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_kv_len_differs_from_queries(ctx, D):
+    """kv_seq_len: 300 queries over two key blocks of 130 and 611 keys (both
+    ragged), the second merged into the first; the K/V of each block are
+    strided views into one buffer of all 741 keys, as the ring's received
+    blocks are. Equals attention over all 741 keys."""
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(40 + D)
+    S, T1, T2, H = 300, 130, 611, 3
+    T = T1 + T2
+    q = rng.standard_normal((S, H, D)).astype(np.float16).astype(np.float32)
+    k = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    v = rng.standard_normal((T, H, D)).astype(np.float16).astype(np.float32)
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=D ** -0.5, layout=L.BHSD)
+    qh = dev(q.transpose(1, 0, 2)).half().contiguous()          # [H, S, D]
+    kh = dev(k.transpose(1, 0, 2)).half().contiguous()          # [H, T, D]
+    vh = dev(v.transpose(1, 0, 2)).half().contiguous()
+    o = torch.empty((S, H * D), device="cuda")
+    lse = torch.empty((H, S), device="cuda")
+    for i, (a, n) in enumerate(((0, T1), (T1, T2))):
+        st = {"k_row_stride": D, "v_row_stride": D, "k_head_stride": T * D,
+              "v_head_stride": T * D}
+        L.attention_fused(ctx, qh, kh[:, a:a + n], vh[:, a:a + n], o, cfg, batch=1, seq_len=S,
+                          lse=lse, merge=i > 0, kv_len=n, strides=st)
+    ctx.sync()
+    s = np.einsum("shd,thd->hst", q.astype(np.float64), k.astype(np.float64)) * D ** -0.5
+    mx = s.max(-1, keepdims=True)
+    p = np.exp(s - mx)
+    want = np.einsum("hst,thd->shd", p / p.sum(-1, keepdims=True),
+                     v.astype(np.float64)).reshape(S, H * D)
+    check(host(o), want, what=f"kv_len D={D}")
+    want_lse = (mx + np.log(p.sum(-1, keepdims=True)))[..., 0]
+    assert np.abs(host(lse) - want_lse).max() < 1e-3
+    # a different key count with a prologue (norm) is rejected
+    bad = L.AttnConfig(n_heads=H, head_dim=D, scale=0.1, layout=L.BHSD, norm_q=True)
+    g = torch.ones(D, device="cuda")
+    ctx.reserve(3 * H * S * D * 2)
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_fused(ctx, qh, kh, vh, o, bad, batch=1, seq_len=S, q_gain=g, kv_len=T)
     assert ei.value.status == L.EINVAL
 
 
