@@ -43,6 +43,10 @@ def parse():
     ap.add_argument("--mode", choices=["batch", "headsplit", "ring"], default="batch",
                     help="batch: one batch element per rank (default, weak scaling); "
                          "headsplit / ring: one attention over all ranks (strong scaling)")
+    ap.add_argument("--matrix", default="",
+                    help="strong-scaling runs in one process group: comma-separated "
+                         "config:mode[:transport] entries, e.g. "
+                         "qwen_edit_2048:ring:copy,flux_1024:headsplit")
     ap.add_argument("--transport", choices=["copy", "nccl"], default="copy",
                     help="ring mode: K/V blocks pulled from their owners on the copy engines "
                          "(copy) or passed around the ring by NCCL P2P (nccl)")
@@ -229,8 +233,33 @@ def run_strong(args):
     scaling): `headsplit` gives each rank a contiguous share of the (b, h)
     units with no communication; `ring` shards the sequence and moves the
     fp16 K/V blocks between ranks (copy engines or NCCL P2P, --transport)
-    while each rank computes.
+    while each rank computes. With --matrix, every listed (config, mode,
+    transport) in turn, in one process group.
     Time per step = max over ranks of the CUDA-event time of the call."""
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
+    runs = [(args.config, args.mode, args.transport)]
+    if args.matrix:
+        runs = []
+        for ent in args.matrix.split(","):
+            parts = ent.split(":")
+            runs.append((parts[0], parts[1], parts[2] if len(parts) > 2 else args.transport))
+    for config, mode, transport in runs:
+        strong_case(args, config, mode, transport)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def strong_case(args, config, mode, transport):
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -243,12 +272,7 @@ def run_strong(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
-                                device_id=torch.device(f"cuda:{local}"))
-    case = C.CASES[args.config]
+    case = C.CASES[config]
     prep = C.prepare(case, L.rope_tables)
     B, S, H, D = prep.q.shape
     dt = torch_dtype(case.dtype)
@@ -259,7 +283,7 @@ def run_strong(args):
     with torch.cuda.stream(stream):
         ctx = L.Context(local, stream=stream)
         qg, kg, cos, sin = g32(prep.q_gain), g32(prep.k_gain), g32(prep.cos), g32(prep.sin)
-        if args.mode == "headsplit":
+        if mode == "headsplit":
             q, k, v = (torch.from_numpy(a).to(dev).to(dt) for a in (prep.q, prep.k, prep.v))
             o = torch.empty((B, S, H * D), dtype=dt, device=dev)
             from llmr_attn.dist import partition_units
@@ -282,7 +306,7 @@ def run_strong(args):
                        for a in (prep.q, prep.k, prep.v))
             o = torch.empty((1, s_loc, H * D), dtype=dt, device=dev)
             ring = RingAttention(RingOps(ctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
-                                 dev, transport=args.transport)
+                                 dev, transport=transport)
             def step():
                 ring.forward(q, k, v, o, qg, kg, cos, sin)
             units = H
@@ -315,21 +339,18 @@ def run_strong(args):
             "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
-            "data": "synthetic", "mode": args.mode,
-            "transport": args.transport if args.mode == "ring" else None,
+            "data": "synthetic", "mode": mode,
+            "transport": transport if mode == "ring" else None,
             "config": {"workload": case.name, "batch": B, "n_heads": H, "seq_len": S,
                        "head_dim": D, "units_rank0": units},
             "pct_of_peak_per_gpu": 100.0 * value / world / peak, "peak_source": kind,
             "gpu_launches_rank0": launches}), flush=True)
-    if args.mode == "ring":
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        ring.close()
-    ctx.close()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-        dist.destroy_process_group()
+    if mode == "ring":
+        ring.close()
+    ctx.close()
 
 
 def main():
@@ -343,7 +364,7 @@ def main():
     if args.profile_run:
         profile_run(args)
         return
-    if args.mode != "batch":
+    if args.mode != "batch" or args.matrix:
         run_strong(args)
         return
     import numpy as np
