@@ -50,6 +50,10 @@ def parse():
     ap.add_argument("--transport", choices=["copy", "nccl"], default="copy",
                     help="ring mode: K/V blocks pulled from their owners on the copy engines "
                          "(copy) or passed around the ring by NCCL P2P (nccl)")
+    ap.add_argument("--qkv", action="store_true",
+                    help="the QKV projection with the prologue in its epilogue "
+                         "(llmr_qkv_project) on the configuration's shapes, against a cuBLAS "
+                         "GEMM (torch.matmul) followed by the standalone prologue")
     ap.add_argument("--cpu-table", action="store_true",
                     help="only the CPU baseline: the oracle on all host cores and on 1 core, "
                          "every configuration, a bounded row sample each")
@@ -165,6 +169,77 @@ def config_block(case, n):
             "n_heads": case.n_heads, "seq_len": case.seq_len, "head_dim": case.head_dim,
             "parallelism": f"batch x head partition over {n} GPU(s), no collective",
             "l2": "flushed (256 MiB write) between timed steps"}
+
+
+def qkv_bench(args):
+    """Hidden = H*D (the model width of the reference's blocks): x [B*S, hidden]
+    and W [3*H*D, hidden] in the configuration's dtype, QK-RMSNorm + RoPE as
+    the configuration has them. Times (a) llmr_qkv_project and (b) cuBLAS
+    x @ W^T into a [B*S, 3*H*D] buffer followed by llmr_attention_prologue
+    reading it as three strided views; both produce the attention kernel's
+    fp16 [3][B][H][S][D] input. CUDA events, L2 flushed between steps."""
+    import numpy as np
+    import torch
+
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import attn_config, torch_dtype
+    case = C.CASES[args.config]
+    prep = C.prepare(case, L.rope_tables)
+    B, S, H, D = prep.q.shape
+    hidden = H * D
+    dt = torch_dtype(case.dtype)
+    if dt == torch.float32:
+        raise SystemExit("--qkv needs a 16-bit configuration")
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn((B * S, hidden), device="cuda", generator=g).to(dt)
+    w = (torch.randn((3 * hidden, hidden), device="cuda", generator=g) * hidden ** -0.5).to(dt)
+    cfg = attn_config(case, S)
+    g32 = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a)).cuda()
+    qg, kg, cos, sin = g32(prep.q_gain), g32(prep.k_gain), g32(prep.cos), g32(prep.sin)
+    ctx = L.Context(0)
+    out = torch.empty((3, B, H, S, D), device="cuda", dtype=torch.float16)
+    y = torch.empty((B * S, 3 * hidden), device="cuda", dtype=dt)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    st = {"q_row_stride": 3 * hidden, "k_row_stride": 3 * hidden, "v_row_stride": 3 * hidden,
+          "q_batch_stride": S * 3 * hidden, "k_batch_stride": S * 3 * hidden,
+          "v_batch_stride": S * 3 * hidden}
+
+    def fused():
+        L.qkv_project(ctx, x, w, out, cfg, batch=B, seq_len=S, q_gain=qg, k_gain=kg, cos=cos,
+                      sin=sin)
+
+    def unfused():
+        torch.matmul(x, w.t(), out=y)
+        L.attention_prologue(ctx, y[:, :hidden], y[:, hidden:2 * hidden], y[:, 2 * hidden:],
+                             out, cfg, batch=B, seq_len=S, q_gain=qg, k_gain=kg, cos=cos,
+                             sin=sin, strides=st)
+
+    res = {}
+    for name, fn in (("fused", fused), ("cublas_plus_prologue", unfused)):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        res[name] = sum(ts) / len(ts)
+    flops = 2.0 * B * S * hidden * 3 * hidden
+    peak, _, kind = peaks()
+    print(json.dumps({
+        "qkv_projection": case.name, "M": B * S, "N": 3 * hidden, "K": hidden,
+        "dtype": case.dtype, "fused_ms": res["fused"],
+        "fused_tflops": flops / (res["fused"] / 1e3) / 1e12,
+        "cublas_plus_prologue_ms": res["cublas_plus_prologue"],
+        "speedup": res["cublas_plus_prologue"] / res["fused"],
+        "peak": peak, "peak_source": kind, "steps": args.steps}), flush=True)
+    ctx.close()
 
 
 def cpu_table(args):
@@ -360,6 +435,9 @@ def main():
         return
     if args.cpu_table:
         cpu_table(args)
+        return
+    if args.qkv:
+        qkv_bench(args)
         return
     if args.profile_run:
         profile_run(args)

@@ -235,6 +235,32 @@ typedef struct {
   uint32_t kv_seq_len;
 } llmr_attn_desc;
 
+/* ---- QKV projection with the prologue in its epilogue --------------------
+ * The step before the path (the reference's three batch matmuls of a block,
+ * dependencies/zimage.c3l/dit.c3:1437-1442 / flux.c3l/flux_dit.c3:787-801,
+ * with the fp16 coopmat GEMM of dependencies/llm_text.c3l/shaders/
+ * llm.slang:2039-2105, followed by batch_head_norm and mrope) as one
+ * tensor-core GEMM: qkv_out[t][b][h][s][d] = epilogue_t(x[b*S+s, :] .
+ * w[t*H*D + h*D + d, :]) written as dense fp16 [3][B][H][S][D] — exactly the
+ * input llmr_attention_fused takes with layout BHSD, in_dtype F16 and no
+ * NORM/ROPE flags (q, k, v at element offsets 0, B*H*S*D, 2*B*H*S*D). For
+ * Q and K the epilogue applies LLMR_NORM_Q / LLMR_NORM_K (gain sets split at
+ * split_row) and LLMR_ROPE (table row rope_row_offset + s), in fp32. */
+typedef struct {
+  uint32_t batch, seq_len, hidden, n_heads, head_dim; /* hidden % 64 == 0 */
+  llmr_dtype dtype;   /* of x and w: LLMR_F16 or LLMR_BF16 (the same for both) */
+  uint32_t flags;     /* LLMR_NORM_Q | LLMR_NORM_K | LLMR_ROPE */
+  float eps;
+  uint32_t split_row, rope_row_offset;
+  uint64_t x_row_stride; /* elements between token rows of x; 0 = hidden */
+} llmr_qkv_desc;
+/* x: [batch*seq_len rows][hidden]; w: [3*n_heads*head_dim][hidden] dense;
+ * qkv_out: fp16, 16-byte aligned. n_heads*head_dim must be a multiple of
+ * 128. */
+int llmr_qkv_project(llmr_ctx *ctx, const llmr_qkv_desc *desc, const void *x,
+                     const void *w, const float *q_gain, const float *k_gain,
+                     const float *cos_t, const float *sin_t, void *qkv_out);
+
 /* Workspace bytes llmr_attention_fused needs for `desc`. */
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *desc);
 

@@ -84,11 +84,6 @@ inline dim3 fa_grid(FaParams &p, int B, int num_sms) {
   return dim3(p.units < sms ? p.units : sms);
 }
 
-// Keeps every use of registers filled by tcgen05.ld after tcgen05.wait::ld.
-__device__ __forceinline__ void reg_fence32(uint32_t *r) {
-#pragma unroll
-  for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
-}
 
 // Which of the 16 exponential pairs of a 32-column chunk are computed on the
 // FMA pipe (exp2_poly_x2) instead of MUFU ex2: bit i set = pair i. Sharing

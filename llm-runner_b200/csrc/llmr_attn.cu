@@ -21,6 +21,7 @@
 #include "../../include/llmr_attn.h"
 #include "fa_tc.cuh"
 #include "kernels_misc.cuh"
+#include "qkv_proj.cuh"
 
 using namespace llmr;
 
@@ -108,6 +109,47 @@ int make_map(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return LLMR_OK;
+}
+
+// 2-D 16-bit tensor map over `rows` rows of `inner` elements (row stride
+// `row_stride` elements) with a 64 x box_rows box and 128-byte swizzle.
+int make_map2d(llmr_ctx *ctx, CUtensorMap *map, const void *base, long long inner,
+               long long rows, long long row_stride, int box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((row_stride * 2) & 15))
+    return fail(ctx, LLMR_EINVAL, "TMA operand base/row stride must be 16-byte aligned");
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_stride * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LLMR_OK;
+}
+
+template <int D, int BN, bool BF16>
+int launch_qkv(llmr_ctx *ctx, const void *x, long long x_rs, const void *w, QkvParams &p,
+               long long hidden) {
+  using C = QkvCfg<D, BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    CUDA_TRY(ctx, cudaFuncSetAttribute(qkv_proj_kernel<D, BN, BF16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set = true;
+  }
+  CUtensorMap mx, mw;
+  int rc;
+  if ((rc = make_map2d(ctx, &mx, x, hidden, p.M, x_rs, C::BM))) return rc;
+  if ((rc = make_map2d(ctx, &mw, w, hidden, 3LL * p.H * D, hidden, BN))) return rc;
+  const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+  const int grid = p.tiles < sms ? p.tiles : sms;
+  qkv_proj_kernel<D, BN, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mx, mw, p);
+  return after_launch(ctx, "qkv_proj");
 }
 
 template <int D, typename OutT>
@@ -444,6 +486,63 @@ int llmr_copy2d_async(llmr_ctx *ctx, void *dst, size_t dpitch, const void *src, 
   cudaStream_t s = stream ? (cudaStream_t)stream : ctx->stream;
   CUDA_TRY(ctx, cudaMemcpy2DAsync(dst, dpitch, src, spitch, width, height, cudaMemcpyDefault, s));
   return LLMR_OK;
+}
+
+int llmr_qkv_project(llmr_ctx *ctx, const llmr_qkv_desc *d, const void *x, const void *w,
+                     const float *q_gain, const float *k_gain, const float *cos_t,
+                     const float *sin_t, void *qkv_out) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!d || !x || !w || !qkv_out) return fail(ctx, LLMR_EINVAL, "null argument");
+  const long long B = d->batch, S = d->seq_len, K = d->hidden, H = d->n_heads, D = d->head_dim;
+  if (B < 1 || S < 1 || H < 1 || K < 64) return fail(ctx, LLMR_EINVAL, "empty problem");
+  if (D != 64 && D != 128) return fail(ctx, LLMR_EINVAL, "head_dim %lld unsupported (64 or 128)", D);
+  if (K % 64) return fail(ctx, LLMR_EINVAL, "hidden must be a multiple of 64");
+  if ((H * D) % 128) return fail(ctx, LLMR_EINVAL, "n_heads*head_dim must be a multiple of 128");
+  if (d->dtype != LLMR_F16 && d->dtype != LLMR_BF16)
+    return fail(ctx, LLMR_EINVAL, "x and w must be fp16 or bf16");
+  if (d->flags & ~(uint32_t)(LLMR_NORM_Q | LLMR_NORM_K | LLMR_ROPE))
+    return fail(ctx, LLMR_EINVAL, "only NORM_Q, NORM_K and ROPE apply to the projection");
+  if ((d->flags & LLMR_NORM_Q) && !q_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_Q needs q_gain");
+  if ((d->flags & LLMR_NORM_K) && !k_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_K needs k_gain");
+  if ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) return fail(ctx, LLMR_EINVAL, "LLMR_ROPE needs cos/sin tables");
+  auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  if (!a16(qkv_out) || (q_gain && !a16(q_gain)) || (k_gain && !a16(k_gain)) ||
+      (cos_t && !a16(cos_t)) || (sin_t && !a16(sin_t)))
+    return fail(ctx, LLMR_EINVAL, "qkv_out, gains and tables must be 16-byte aligned");
+  if (B * S > 0x7fffffffLL || 3 * B * H * S * D > (1LL << 40))
+    return fail(ctx, LLMR_EINVAL, "problem too large");
+  const long long x_rs = d->x_row_stride ? (long long)d->x_row_stride : K;
+  QkvParams p;
+  p.M = (int)(B * S);
+  p.S = (int)S;
+  p.B = (int)B;
+  p.H = (int)H;
+  p.k_blocks = (int)(K / 64);
+  p.split_row = (int)d->split_row;
+  p.rope_row_offset = (int)d->rope_row_offset;
+  p.eps = d->eps;
+  p.q_gain = (d->flags & LLMR_NORM_Q) ? q_gain : nullptr;
+  p.k_gain = (d->flags & LLMR_NORM_K) ? k_gain : nullptr;
+  p.cos_t = (d->flags & LLMR_ROPE) ? cos_t : nullptr;
+  p.sin_t = (d->flags & LLMR_ROPE) ? sin_t : nullptr;
+  p.out = static_cast<__half *>(qkv_out);
+  p.err = ctx->d_err;
+  const bool bf = d->dtype == LLMR_BF16;
+  const bool wide = (H * D) % 256 == 0;  // 256-column tiles (two or four heads)
+  const int BN = wide ? 256 : 128;
+  p.n_tiles = (int)(3 * H * D / BN);
+  p.tiles = (int)((p.M + 127) / 128) * p.n_tiles;
+  if (D == 128) {
+    if (wide) return bf ? launch_qkv<128, 256, true>(ctx, x, x_rs, w, p, K)
+                        : launch_qkv<128, 256, false>(ctx, x, x_rs, w, p, K);
+    return bf ? launch_qkv<128, 128, true>(ctx, x, x_rs, w, p, K)
+              : launch_qkv<128, 128, false>(ctx, x, x_rs, w, p, K);
+  }
+  if (wide) return bf ? launch_qkv<64, 256, true>(ctx, x, x_rs, w, p, K)
+                      : launch_qkv<64, 256, false>(ctx, x, x_rs, w, p, K);
+  return bf ? launch_qkv<64, 128, true>(ctx, x, x_rs, w, p, K)
+            : launch_qkv<64, 128, false>(ctx, x, x_rs, w, p, K);
 }
 
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {

@@ -120,6 +120,22 @@ __device__ __forceinline__ void tma_load_4d(void *smem_dst,
       : "memory");
 }
 
+// 2-D tiled bulk tensor load (c0 innermost).
+__device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *map,
+                                            uint64_t *bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Keeps every use of registers filled by tcgen05.ld after tcgen05.wait::ld.
+__device__ __forceinline__ void reg_fence32(uint32_t *r) {
+#pragma unroll
+  for (int i = 0; i < 32; i++) asm volatile("" : "+r"(r[i]));
+}
+
 // ------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t ncols) {
   asm volatile(
@@ -278,6 +294,11 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo,
 __host__ __device__ constexpr uint32_t idesc_f16_f32(uint32_t M, uint32_t N,
                                                      uint32_t b_mn_major) {
   return (1u << 4) | (b_mn_major << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+// kind::f16 with fp32 accumulation, both operands K-major, A and B of the
+// same format: 0 = fp16, 1 = bf16 (bits 7-9 and 10-12).
+__host__ __device__ constexpr uint32_t idesc_mma_f32(uint32_t M, uint32_t N, uint32_t ab_fmt) {
+  return (1u << 4) | (ab_fmt << 7) | (ab_fmt << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 // ------------------------------------------------------------------ math

@@ -1,0 +1,299 @@
+// QKV projection with the attention prologue in its epilogue, for sm_100a:
+//
+//   out[t][b][h][s][:] = epi_t( x[b, s, :] . W[t*H*D + h*D + d, :] )   d < D
+//
+// x [B*S, hidden] and W [3*H*D, hidden] (the reference's [out_dim, in_dim]
+// row-major weight convention, dependencies/llm_text.c3l/shaders/
+// llm.slang:1198-1232 batch_matmul_f16 and :2039-2105
+// batch_matmul_f16_coopmat: fp16 operands, fp32 accumulation; rows
+// Q = 0, K = dim, V = 2*dim via row_offset, dependencies/zimage.c3l/
+// dit.c3:1437-1442) are both fp16 or both bf16. epi_t is, for Q and K, the
+// per-head RMSNorm with the txt/img gain split (zimage.slang:623-659) and the
+// interleaved RoPE rotation (mrope.slang:47-53), in fp32 with the same
+// operation order as the standalone prologue; for V the identity. The
+// result is written as fp16 in the dense [3][B][H][S][D] layout the
+// attention kernel reads, so the attention call that follows needs no
+// prologue.
+//
+// CTA (persistent, one per SM) = 192 threads:
+//   warp 0     TMA producer: x (128 x 64) and W (BN x 64) tiles into a
+//              4-stage ring of SW128 buffers
+//   warp 1     TMEM owner and MMA issuer (tcgen05.mma M128 x BN x 16, fp32
+//              accumulators, two BN-column buffers so one tile's epilogue
+//              overlaps the next tile's main loop)
+//   warps 2-5  epilogue: thread = accumulator row (TMEM lane); for each head
+//              of the tile a first pass over its columns gives the RMS, a
+//              second pass normalises, rotates, rounds to fp16 and stores 32
+//              columns at a time (one contiguous 2*D-byte row per thread).
+#pragma once
+#include <cuda_fp16.h>
+
+#include "ptx.cuh"
+
+namespace llmr {
+
+struct QkvParams {
+  int M;                 // B * S token rows
+  int S;                 // tokens per batch element
+  int B, H;
+  int k_blocks;          // hidden / 64
+  int n_tiles;           // 3 * H * D / BN
+  int tiles;             // ceil(M / 128) * n_tiles
+  int split_row;         // global token index from which gain set 1 applies
+  int rope_row_offset;   // global token index of token 0
+  float eps;
+  const float *q_gain, *k_gain;  // [D] or [2][D]; null = no norm
+  const float *cos_t, *sin_t;    // [rows][D/2]; null = no RoPE
+  __half *out;                   // [3][B][H][S][D]
+  int *err;
+};
+
+template <int D, int BN>
+struct QkvCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+  static constexpr int B_BYTES = BN * BK * 2;  // 16 or 32 KB
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int NST = BN == 256 ? 4 : 6;
+  static constexpr int BAR_OFF = NST * STAGE_BYTES;
+  // barriers: full[NST], empty[NST], acc_full[2], acc_empty[2], drain; then
+  // the tmem base word and the abort flag
+  static constexpr int NBAR = 2 * NST + 2 + 2 + 1;
+  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
+  static constexpr int THREADS = 192;
+  static constexpr uint32_t TMEM_COLS = 2 * BN;
+  static constexpr int HEADS_PER_TILE = BN / D;
+};
+
+template <int D, int BN, bool BF16>
+__global__ void __launch_bounds__(192, 1)
+    qkv_proj_kernel(const __grid_constant__ CUtensorMap tmX,
+                    const __grid_constant__ CUtensorMap tmW, const QkvParams p) {
+  using C = QkvCfg<D, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+  uint64_t *full = bars;
+  uint64_t *empty = full + C::NST;
+  uint64_t *acc_full = empty + C::NST;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tiles = (p.M + C::BM - 1) / C::BM;
+  // Tile order: groups of kGroupM row blocks, each group walked m-fastest
+  // over all column blocks, so the CTAs running together (about one per SM)
+  // share a few x row blocks and W column blocks in L2 instead of streaming
+  // all of x from DRAM once per column block.
+  constexpr int kGroupM = 16;
+  auto decode = [&](int tile, int &m0, int &n0) {
+    const int per_group = kGroupM * p.n_tiles;
+    const int grp = tile / per_group;
+    const int first = grp * kGroupM;
+    const int gm = m_tiles - first < kGroupM ? m_tiles - first : kGroupM;
+    const int in = tile - grp * per_group;
+    m0 = (first + in % gm) * C::BM;
+    n0 = (in / gm) * BN;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NST; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      tma_prefetch_desc(&tmW);
+      bool ok = true;
+      int it = 0;  // stage loads armed so far (over all tiles)
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+        int m0, n0;
+        decode(tile, m0, n0);
+        for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+          const int st = it % C::NST, round = it / C::NST;
+          if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + st * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+          tma_load_2d(sa, &tmX, &full[st], kb * C::BK, m0);
+          tma_load_2d(sa + C::A_BYTES, &tmW, &full[st], kb * C::BK, n0);
+        }
+      }
+      if (!ok) {
+        for (int u = it - C::NST < 0 ? 0 : it - C::NST; u < it; u++)
+          mbar_wait_raw(&full[u % C::NST], (u / C::NST) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    constexpr uint32_t IDESC = idesc_mma_f32(C::BM, BN, BF16 ? 1u : 0u);
+    const uint32_t sbase = smem_u32(smem);
+    bool ok = true;
+    int it = 0;
+    int local = 0;  // tiles of this CTA so far
+    for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, local++) {
+      const int buf = local & 1;
+      // The epilogue must have read this accumulator buffer (two tiles ago).
+      if (local >= 2 && !(ok = mbar_wait(&acc_empty[buf], ((local >> 1) - 1) & 1, abort_flag)))
+        break;
+      tc_fence_after();
+      for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+        const int st = it % C::NST;
+        if (!(ok = mbar_wait(&full[st], (it / C::NST) & 1, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t a = sbase + st * C::STAGE_BYTES;
+        const uint32_t b = a + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; kk++) {
+          if (elect_one())
+            mma_ss(tmem + buf * BN, sdesc_sw128(a + kk * 32, 16, 1024),
+                   sdesc_sw128(b + kk * 32, 16, 1024), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (elect_one()) mma_commit(&empty[st]);
+      }
+      if (!ok) break;
+      if (elect_one()) mma_commit(&acc_full[buf]);
+    }
+    if (elect_one()) mma_commit(drain);
+    mbar_wait_raw(drain, 0, 100000000ull);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // warps 2..5 -> TMEM lane quarters 2,3,0,1
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const long long plane = (long long)p.B * p.H * p.S * D;
+    const int hd = p.H * D;
+    bool ok = true;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, local++) {
+      const int buf = local & 1;
+      int m0, n0;
+      decode(tile, m0, n0);
+      ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (local >> 1) & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const int m = m0 + row;
+      const bool in = m < p.M;
+      const int b = in ? m / p.S : 0;
+      const int s = in ? m - b * p.S : 0;
+      const long long grow = (long long)p.rope_row_offset + s;
+      const int t = n0 / hd;  // 0 = Q, 1 = K, 2 = V (a tile never spans two)
+      const float *gain = t == 0 ? p.q_gain : (t == 1 ? p.k_gain : nullptr);
+      const bool rope = t < 2 && p.cos_t != nullptr;
+#pragma unroll 1
+      for (int hl = 0; hl < C::HEADS_PER_TILE; hl++) {
+        const int h = (n0 - t * hd) / D + hl;
+        const uint32_t tacc = tmem + lane_off + buf * BN + hl * D;
+        // Pass 1 (Q/K with norm): the row's sum of squares, chunk by chunk.
+        float rms = 1.0f;
+        if (gain != nullptr) {
+          float ss = 0.0f;
+#pragma unroll 1
+          for (int c = 0; c < D / 32; c++) {
+            uint32_t r[32];
+            tmem_ld32(tacc + c * 32, r);
+            tmem_wait_ld();
+            reg_fence32(r);
+#pragma unroll
+            for (int e = 0; e < 32; e++) ss = __fmaf_rn(__uint_as_float(r[e]), __uint_as_float(r[e]), ss);
+          }
+          rms = rsqrtf(ss / (float)D + p.eps);
+        }
+        const float *g = gain == nullptr ? nullptr
+                                         : gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0);
+        const float *ct = p.cos_t + grow * (D / 2);
+        const float *stt = p.sin_t + grow * (D / 2);
+        __half *dst = p.out + t * plane + (((long long)b * p.H + h) * p.S + s) * D;
+        // Pass 2: 32 columns at a time: norm, rotation, fp16, store.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; c++) {
+          uint32_t r[32];
+          tmem_ld32(tacc + c * 32, r);
+          tmem_wait_ld();
+          reg_fence32(r);
+          if (hl == C::HEADS_PER_TILE - 1 && c == D / 32 - 1) {
+            // The accumulator buffer is read out: the MMA warp may reuse it.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[buf]);
+          }
+          float y[32];
+#pragma unroll
+          for (int e = 0; e < 32; e++) y[e] = __uint_as_float(r[e]);
+          if (g != nullptr) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const float4 gv = *reinterpret_cast<const float4 *>(g + c * 32 + e);
+              y[e] = __fmul_rn(__fmul_rn(y[e], rms), gv.x);
+              y[e + 1] = __fmul_rn(__fmul_rn(y[e + 1], rms), gv.y);
+              y[e + 2] = __fmul_rn(__fmul_rn(y[e + 2], rms), gv.z);
+              y[e + 3] = __fmul_rn(__fmul_rn(y[e + 3], rms), gv.w);
+            }
+          }
+          if (rope && in) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              const float4 cv = *reinterpret_cast<const float4 *>(ct + (c * 32 + e) / 2);
+              const float4 sv = *reinterpret_cast<const float4 *>(stt + (c * 32 + e) / 2);
+              const float cc[4] = {cv.x, cv.y, cv.z, cv.w};
+              const float sn[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+              for (int i = 0; i < 8; i += 2) {
+                const float x0 = y[e + i], x1 = y[e + i + 1];
+                y[e + i] = __fsub_rn(__fmul_rn(x0, cc[i / 2]), __fmul_rn(x1, sn[i / 2]));
+                y[e + i + 1] = __fadd_rn(__fmul_rn(x0, sn[i / 2]), __fmul_rn(x1, cc[i / 2]));
+              }
+            }
+          }
+          if (in) {
+#pragma unroll
+            for (int e = 0; e < 32; e += 8) {
+              uint4 u;
+              u.x = pack_f16x2(y[e], y[e + 1]);
+              u.y = pack_f16x2(y[e + 2], y[e + 3]);
+              u.z = pack_f16x2(y[e + 4], y[e + 5]);
+              u.w = pack_f16x2(y[e + 6], y[e + 7]);
+              *reinterpret_cast<uint4 *>(dst + c * 32 + e) = u;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
+}
+
+}  // namespace llmr

@@ -70,6 +70,17 @@ class AttnDesc(ctypes.Structure):
     ]
 
 
+class QkvDesc(ctypes.Structure):
+    """llmr_qkv_desc (include/llmr_attn.h)."""
+    _fields_ = [
+        ("batch", ctypes.c_uint32), ("seq_len", ctypes.c_uint32),
+        ("hidden", ctypes.c_uint32), ("n_heads", ctypes.c_uint32),
+        ("head_dim", ctypes.c_uint32), ("dtype", ctypes.c_int), ("flags", ctypes.c_uint32),
+        ("eps", ctypes.c_float), ("split_row", ctypes.c_uint32),
+        ("rope_row_offset", ctypes.c_uint32), ("x_row_stride", ctypes.c_uint64),
+    ]
+
+
 class IpcHandle(ctypes.Structure):
     """llmr_ipc_handle: an exported device allocation (64 opaque bytes)."""
     _fields_ = [("bytes", ctypes.c_ubyte * 64)]
@@ -116,6 +127,7 @@ def _load() -> ctypes.CDLL:
         "llmr_attention_fused_noalloc": (i32, [ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                                vp, vp, vp, vp, vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
+        "llmr_qkv_project": (i32, [vp, ctypes.POINTER(QkvDesc), vp, vp, vp, vp, vp, vp, vp]),
         "llmr_ipc_export": (i32, [vp, vp, ctypes.POINTER(IpcHandle)]),
         "llmr_ipc_open": (i32, [vp, ctypes.POINTER(IpcHandle), ctypes.POINTER(vp)]),
         "llmr_ipc_close": (i32, [vp, vp]),
@@ -374,6 +386,30 @@ def attention_merge(ctx: Context, o_a, lse_a, o_b, lse_b, rows: int, n_heads: in
                                        _ptr(lse_b), rows, n_heads, head_dim, o_row_stride))
 
 
+# -------------------------------------------------------------- QKV projection
+
+def qkv_project(ctx: Context, x, w, qkv_out, cfg: AttnConfig, *, batch: int, seq_len: int,
+                q_gain=None, k_gain=None, cos=None, sin=None) -> None:
+    """qkv_out (fp16 [3, B, H, S, D]) <- x [B*S, hidden] . w[3*H*D, hidden]^T
+    with cfg's RMSNorm (norm_q / norm_k, eps, split_row) and RoPE
+    (rope, rope_row_offset) applied to Q and K in the epilogue. x and w are
+    both fp16 or both bf16. The result feeds attention_fused with
+    layout=BHSD, fp16 inputs and no norm/RoPE flags."""
+    d = QkvDesc()
+    d.batch, d.seq_len, d.hidden = batch, seq_len, x.shape[-1]
+    d.n_heads, d.head_dim = cfg.n_heads, cfg.head_dim
+    d.dtype = _dtype_code(x)
+    d.flags = ((NORM_Q if cfg.norm_q else 0) | (NORM_K if cfg.norm_k else 0)
+               | (ROPE if cfg.rope else 0))
+    d.eps, d.split_row, d.rope_row_offset = cfg.eps, cfg.split_row, cfg.rope_row_offset
+    d.x_row_stride = x.stride(-2) if x.dim() >= 2 else 0
+    if _dtype_code(w) != d.dtype:
+        raise LlmrError(EINVAL, "x and w must have the same dtype")
+    ctx.check(lib.llmr_qkv_project(ctx.handle, ctypes.byref(d), _ptr(x), _ptr(w),
+                                   _ptr(q_gain), _ptr(k_gain), _ptr(cos), _ptr(sin),
+                                   _ptr(qkv_out)))
+
+
 # --------------------------------------------------------------------- peer buffers
 
 _TYPESTR = {"float16": "<f2", "bfloat16": None, "float32": "<f4", "uint8": "|u1"}
@@ -480,6 +516,6 @@ __all__ = [
     "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
     "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
     "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
-    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "IpcHandle", "LIB_PATH",
+    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "qkv_project", "QkvDesc", "IpcHandle", "LIB_PATH",
     "lib",
 ]

@@ -32,14 +32,18 @@ def test_library_exports_every_declared_symbol():
     assert not missing, missing
 
 
-def test_desc_layout_matches_c():
-    """ctypes AttnDesc has the C struct's size and field offsets."""
+@pytest.mark.parametrize("py_name,c_name", [("AttnDesc", "llmr_attn_desc"),
+                                             ("QkvDesc", "llmr_qkv_desc"),
+                                             ("IpcHandle", "llmr_ipc_handle")])
+def test_desc_layout_matches_c(py_name, c_name):
+    """The ctypes structs have the C structs' sizes and field offsets."""
     import llmr_attn
-    fields = [f[0] for f in llmr_attn.AttnDesc._fields_]
+    cls = getattr(llmr_attn, py_name)
+    fields = [f[0] for f in cls._fields_]
     src = '#include <stdio.h>\n#include <stddef.h>\n#include "' + HEADER + '"\nint main(){'
-    src += 'printf("%zu\\n", sizeof(llmr_attn_desc));'
+    src += 'printf("%zu\\n", sizeof(' + c_name + '));'
     for f in fields:
-        src += 'printf("%zu\\n", offsetof(llmr_attn_desc, ' + f + '));'
+        src += 'printf("%zu\\n", offsetof(' + c_name + ', ' + f + '));'
     src += "return 0;}"
     with tempfile.TemporaryDirectory() as td:
         c = os.path.join(td, "t.c")
@@ -49,9 +53,9 @@ def test_desc_layout_matches_c():
         subprocess.run([cc, c, "-o", exe], check=True)
         vals = [int(x) for x in subprocess.run([exe], capture_output=True, text=True,
                                                check=True).stdout.split()]
-    assert vals[0] == ctypes.sizeof(llmr_attn.AttnDesc)
+    assert vals[0] == ctypes.sizeof(cls)
     for f, off in zip(fields, vals[1:]):
-        assert getattr(llmr_attn.AttnDesc, f).offset == off, f
+        assert getattr(cls, f).offset == off, f
 
 
 @pytest.mark.parametrize("axes,theta", [((16, 56, 56), 10000.0), ((32, 48, 48), 256.0),
