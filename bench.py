@@ -47,6 +47,8 @@ def parse():
                     help="strong-scaling runs in one process group: comma-separated "
                          "config:mode[:transport] entries, e.g. "
                          "qwen_edit_2048:ring:copy,flux_1024:headsplit")
+    ap.add_argument("--copy-streams", type=int, default=1,
+                    help="ring copy transport: side streams (copy engines) per pull")
     ap.add_argument("--transport", choices=["copy", "nccl"], default="copy",
                     help="ring mode: K/V blocks pulled from their owners on the copy engines "
                          "(copy) or passed around the ring by NCCL P2P (nccl)")
@@ -321,20 +323,22 @@ def run_strong(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device(f"cuda:{local}"))
-    runs = [(args.config, args.mode, args.transport)]
     if args.matrix:
         runs = []
         for ent in args.matrix.split(","):
             parts = ent.split(":")
-            runs.append((parts[0], parts[1], parts[2] if len(parts) > 2 else args.transport))
-    for config, mode, transport in runs:
-        strong_case(args, config, mode, transport)
+            runs.append((parts[0], parts[1], parts[2] if len(parts) > 2 else args.transport,
+                         int(parts[3]) if len(parts) > 3 else args.copy_streams))
+    else:
+        runs = [(args.config, args.mode, args.transport, args.copy_streams)]
+    for config, mode, transport, copy_streams in runs:
+        strong_case(args, config, mode, transport, copy_streams)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
-def strong_case(args, config, mode, transport):
+def strong_case(args, config, mode, transport, copy_streams=1):
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -380,7 +384,8 @@ def strong_case(args, config, mode, transport):
             q, k, v = (torch.from_numpy(np.ascontiguousarray(a[:, sl])).to(dev).to(dt)
                        for a in (prep.q, prep.k, prep.v))
             o = torch.empty((1, s_loc, H * D), dtype=dt, device=dev)
-            ring = RingAttention(RingOps(ctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
+            ring = RingAttention(RingOps(ctx, cfg, s_loc, rank * s_loc,
+                                         copy_streams=copy_streams), H, D, S, rank, world,
                                  dev, transport=transport)
             def step():
                 ring.forward(q, k, v, o, qg, kg, cos, sin)
@@ -416,6 +421,7 @@ def strong_case(args, config, mode, transport):
             "scaling": "strong", "vs_baseline": None, "dtype": case.dtype,
             "data": "synthetic", "mode": mode,
             "transport": transport if mode == "ring" else None,
+            "copy_streams": copy_streams if mode == "ring" and transport == "copy" else None,
             "config": {"workload": case.name, "batch": B, "n_heads": H, "seq_len": S,
                        "head_dim": D, "units_rank0": units},
             "pct_of_peak_per_gpu": 100.0 * value / world / peak, "peak_source": kind,

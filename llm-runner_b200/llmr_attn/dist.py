@@ -22,7 +22,7 @@ Two schemes, both new relative to the reference (which is single-GPU,
     gives every pair full bandwidth, so no block is passed on hop by hop.
     Received blocks are stored so that each head's keys of all blocks are
     contiguous, and the kernel covers groups of arrived blocks in one launch
-    (`ring_groups`: own block, then 2, 4, ... blocks). A second barrier
+    (`ring_groups`: own block, then 1, 1, 2, 3, ... blocks). A second barrier
     after the pulls lets owners overwrite their block in the next call.
   - "nccl": the classic ring: the current block goes to rank r+1 and the
     next one comes from rank r-1 by NCCL P2P (batch_isend_irecv) each step.
@@ -87,8 +87,9 @@ class RingOps:
     """The device steps of the ring, on the library's CUDA kernels."""
 
     def __init__(self, ctx: "L.Context", cfg: "L.AttnConfig", seq_local: int,
-                 row_offset: int):
+                 row_offset: int, copy_streams: int = 1):
         self.ctx, self.cfg, self.S, self.off = ctx, cfg, seq_local, row_offset
+        self.n_copy = max(1, copy_streams)
         self.part_cfg = L.AttnConfig(n_heads=cfg.n_heads, head_dim=cfg.head_dim,
                                      scale=cfg.scale, layout=L.BHSD)
 
@@ -134,7 +135,10 @@ class RingOps:
         self.kv_bytes = 2 * self.kv_offset
         self.group = group
         self.compute = torch.cuda.current_stream()
-        self.comm = torch.cuda.Stream()
+        # Side streams for the pulls: copies on different streams run on
+        # different copy engines at once. comm[0] also carries the barriers.
+        self.comm_streams = [torch.cuda.Stream() for _ in range(self.n_copy)]
+        self.comm = self.comm_streams[0]
         self.tok = torch.zeros(1, device=device)
         self.released = None
         return self.own.tensor(shape, dtype)
@@ -156,6 +160,8 @@ class RingOps:
         after every rank's prologue: peers' blocks are complete after it."""
         self.comm.wait_stream(self.compute)
         self._barrier_on_comm()
+        for st in self.comm_streams[1:]:
+            st.wait_stream(self.comm)
 
     def fetch(self, src_rank, slot, kv_recv):
         """Copies rank src_rank's K/V block ([2][H][S][D]) into slot `slot` of
@@ -167,21 +173,36 @@ class RingOps:
         S = self.S
         esize = kv_recv.element_size()
         row = S * D * esize                       # one head of one block
+        # K and V, each cut into head ranges, spread over the side streams
+        parts = []
+        per = max(1, (2 * len(self.comm_streams)) // 2)
         for i in range(2):
-            dst = kv_recv[i].data_ptr() + slot * row
-            src = self.peers[src_rank].ptr + self.kv_offset + i * H * row
-            L.copy2d_async(self.ctx, dst, T * D * esize, src, row, row, H, self.comm)
-        ev = torch.cuda.Event()
-        ev.record(self.comm)
-        return ev
+            for c in range(per):
+                h0, h1 = c * H // per, (c + 1) * H // per
+                if h1 > h0:
+                    parts.append((i, h0, h1))
+        events = []
+        for n, (i, h0, h1) in enumerate(parts):
+            st = self.comm_streams[n % len(self.comm_streams)]
+            dst = kv_recv[i].data_ptr() + h0 * T * D * esize + slot * row
+            src = self.peers[src_rank].ptr + self.kv_offset + (i * H + h0) * row
+            L.copy2d_async(self.ctx, dst, T * D * esize, src, row, row, h1 - h0, st)
+        for st in self.comm_streams:
+            ev = torch.cuda.Event()
+            ev.record(st)
+            events.append(ev)
+        return events
 
-    def wait(self, ev):
-        self.compute.wait_event(ev)
+    def wait(self, events):
+        for ev in events:
+            self.compute.wait_event(ev)
 
     def release(self):
         """Barrier after this rank's pulls: when every rank has passed it, no
         rank reads this rank's block any more."""
         import torch
+        for st in self.comm_streams[1:]:
+            self.comm.wait_stream(st)
         self._barrier_on_comm()
         self.released = torch.cuda.Event()
         self.released.record(self.comm)
@@ -280,15 +301,16 @@ class RingAttention:
 
 def ring_groups(n: int) -> List[Tuple[int, int]]:
     """Received blocks 0..n-1 as consecutive (first, count) groups of
-    doubling size (2, 4, 8, ...), the last group taking the remainder: one
-    attention launch per group, each starting while the later blocks are
-    still being copied. n=7 -> [(0, 2), (2, 5)]."""
-    groups, i, size = [], 0, 2
+    Fibonacci sizes (1, 1, 2, 3, 5, ...; the last group takes what is left):
+    one attention launch per group. A group only needs blocks that arrived
+    while the previous groups were computed, as long as computing one block
+    takes about as long as pulling one, so the kernel never waits for the
+    copy engines; the growing sizes keep the number of launches small.
+    n=7 -> [(0, 1), (1, 1), (2, 2), (4, 3)]."""
+    groups, i, a, b = [], 0, 1, 1
     while i < n:
-        take = min(size, n - i)
-        if n - (i + take) < 2 * size:
-            take = n - i
+        take = min(a, n - i)
         groups.append((i, take))
         i += take
-        size *= 2
+        a, b = b, a + b
     return groups

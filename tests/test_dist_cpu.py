@@ -39,14 +39,14 @@ def test_ring_groups_cover_in_order(n):
     covered = [i for a, c in groups for i in range(a, a + c)]
     assert covered == list(range(n))
     assert all(c >= 1 for _, c in groups)
-    if n >= 2:
-        assert groups[0] == (0, min(2, n)) or len(groups) == 1
+    sizes = [c for _, c in groups]
+    assert all(sizes[j] <= sizes[j - 1] + (sizes[j - 2] if j >= 2 else 0) for j in range(1, len(sizes)))
 
 
 def test_ring_groups_eight_gpus():
-    assert ring_groups(7) == [(0, 2), (2, 5)]
+    assert ring_groups(7) == [(0, 1), (1, 1), (2, 2), (4, 3)]
     assert ring_groups(1) == [(0, 1)]
-    assert ring_groups(3) == [(0, 3)]
+    assert ring_groups(3) == [(0, 1), (1, 1), (2, 1)]
 
 
 def test_partition_zimage_8_gpus():
