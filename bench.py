@@ -56,6 +56,10 @@ def parse():
                     help="the QKV projection with the prologue in its epilogue "
                          "(llmr_qkv_project) on the configuration's shapes, against a cuBLAS "
                          "GEMM (torch.matmul) followed by the standalone prologue")
+    ap.add_argument("--proj", action="store_true",
+                    help="the output projection with the gated residual in its epilogue "
+                         "(llmr_out_project, txt/img weight sets) against cuBLAS GEMMs per "
+                         "stream followed by torch's bias / gate / residual ops")
     ap.add_argument("--cpu-table", action="store_true",
                     help="only the CPU baseline: the oracle on all host cores and on 1 core, "
                          "every configuration, a bounded row sample each")
@@ -241,6 +245,70 @@ def qkv_bench(args):
         "cublas_plus_prologue_ms": res["cublas_plus_prologue"],
         "speedup": res["cublas_plus_prologue"] / res["fused"],
         "peak": peak, "peak_source": kind, "steps": args.steps}), flush=True)
+    ctx.close()
+
+
+def proj_bench(args):
+    """o [B*S, H*D] (the attention output) and two weight sets [H*D, H*D] in the
+    configuration's dtype, split at the configuration's txt/img row, fp32
+    hidden: (a) llmr_out_project; (b) per stream a cuBLAS GEMM, bias add and
+    gated residual with torch ops. CUDA events, L2 flushed between steps."""
+    import torch
+
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import torch_dtype
+    case = C.CASES[args.config]
+    B, S, H, D = case.batch, case.seq_len, case.n_heads, case.head_dim
+    dim = H * D
+    dt = torch_dtype(case.dtype)
+    if dt == torch.float32:
+        raise SystemExit("--proj needs a 16-bit configuration")
+    split = min(case.split_row, S) if case.split_row else 0
+    g = torch.Generator(device="cuda").manual_seed(9)
+    o = torch.randn((B * S, dim), device="cuda", generator=g).to(dt)
+    w = [(torch.randn((dim, dim), device="cuda", generator=g) * dim ** -0.5).to(dt)
+         for _ in range(2)]
+    bias = [torch.randn(dim, device="cuda", generator=g) for _ in range(2)]
+    gate = [torch.rand(dim, device="cuda", generator=g) for _ in range(2)]
+    hidden = torch.randn((B * S, dim), device="cuda", generator=g)
+    ctx = L.Context(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    o3, h3 = o.view(B, S, dim), hidden.view(B, S, dim)
+    segs = [(0, split, 0), (split, S, 1)] if split else [(0, S, 0)]
+
+    def fused():
+        L.out_project(ctx, o, hidden, w[0], w[1] if split else None, batch=B, seq_len=S,
+                      split_row=split, bias0=bias[0], bias1=bias[1], gate0=gate[0],
+                      gate1=gate[1])
+
+    def unfused():
+        for s0, s1, k in segs:
+            y = torch.matmul(o3[:, s0:s1], w[k].t()).float()
+            h3[:, s0:s1] += gate[k] * (y + bias[k])
+
+    res = {}
+    for name, fn in (("fused", fused), ("cublas_plus_torch", unfused)):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        res[name] = sum(ts) / len(ts)
+    flops = 2.0 * B * S * dim * dim
+    print(json.dumps({
+        "out_projection": case.name, "M": B * S, "N": dim, "K": dim, "split_row": split,
+        "dtype": case.dtype, "fused_ms": res["fused"],
+        "fused_tflops": flops / (res["fused"] / 1e3) / 1e12,
+        "cublas_plus_torch_ms": res["cublas_plus_torch"],
+        "speedup": res["cublas_plus_torch"] / res["fused"], "steps": args.steps}), flush=True)
     ctx.close()
 
 
@@ -444,6 +512,9 @@ def main():
         return
     if args.qkv:
         qkv_bench(args)
+        return
+    if args.proj:
+        proj_bench(args)
         return
     if args.profile_run:
         profile_run(args)

@@ -261,6 +261,31 @@ int llmr_qkv_project(llmr_ctx *ctx, const llmr_qkv_desc *desc, const void *x,
                      const void *w, const float *q_gain, const float *k_gain,
                      const float *cos_t, const float *sin_t, void *qkv_out);
 
+/* ---- Output projection with the gated residual in its epilogue ---------
+ * The step after the path: hidden[b*S+s, n] += gate_g[n] *
+ * (o[b*S+s, :] . w_g[n, :] + bias_g[n]) with weight set g = 1 for tokens
+ * s >= split_row when split_row > 0, else g = 0 — the joint blocks' two
+ * streams with their own projection, bias and gate
+ * (dependencies/flux.c3l/flux_dit.c3:874-885, dependencies/qwen_edit.c3l/
+ * mmdit.c3:694-720: matmul, broadcast_bias_add vit.slang:133-137,
+ * gated_residual_add vit.slang:638-647), in one tensor-core GEMM. o is the
+ * attention output [batch*seq_len][in_dim] (fp16 or bf16, e.g. the output of
+ * llmr_attention_fused), w0 / w1 [out_dim][in_dim] dense of o's type (w1
+ * only with split_row > 0), bias / gate fp32 [out_dim] or NULL (0 / 1),
+ * hidden fp32 [batch*seq_len][out_dim] (row stride hidden_row_stride,
+ * 0 = out_dim), updated in place. in_dim % 64 == 0, out_dim % 256 == 0. */
+typedef struct {
+  uint32_t batch, seq_len, in_dim, out_dim;
+  llmr_dtype dtype;    /* of o and the weights: LLMR_F16 or LLMR_BF16 */
+  uint32_t split_row;
+  uint64_t o_row_stride;      /* elements; 0 = in_dim */
+  uint64_t hidden_row_stride; /* elements; 0 = out_dim */
+} llmr_proj_desc;
+int llmr_out_project(llmr_ctx *ctx, const llmr_proj_desc *desc, const void *o,
+                     const void *w0, const void *w1, const float *bias0,
+                     const float *bias1, const float *gate0,
+                     const float *gate1, float *hidden);
+
 /* Workspace bytes llmr_attention_fused needs for `desc`. */
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *desc);
 

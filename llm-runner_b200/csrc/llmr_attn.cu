@@ -152,6 +152,23 @@ int launch_qkv(llmr_ctx *ctx, const void *x, long long x_rs, const void *w, QkvP
   return after_launch(ctx, "qkv_proj");
 }
 
+template <bool BF16>
+int launch_out_proj(llmr_ctx *ctx, const CUtensorMap &mx, const CUtensorMap &mw0,
+                    const CUtensorMap &mw1, const ProjParams &p) {
+  using C = QkvCfg<128, 256>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    CUDA_TRY(ctx, cudaFuncSetAttribute(out_proj_kernel<BF16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kProjSmemBytes));
+    attr_set = true;
+  }
+  const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+  const int grid = p.tiles < sms ? p.tiles : sms;
+  out_proj_kernel<BF16><<<grid, C::THREADS, kProjSmemBytes, ctx->stream>>>(mx, mw0, mw1, p);
+  return after_launch(ctx, "out_proj");
+}
+
 template <int D, typename OutT>
 int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                  const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
@@ -543,6 +560,55 @@ int llmr_qkv_project(llmr_ctx *ctx, const llmr_qkv_desc *d, const void *x, const
                       : launch_qkv<64, 256, false>(ctx, x, x_rs, w, p, K);
   return bf ? launch_qkv<64, 128, true>(ctx, x, x_rs, w, p, K)
             : launch_qkv<64, 128, false>(ctx, x, x_rs, w, p, K);
+}
+
+int llmr_out_project(llmr_ctx *ctx, const llmr_proj_desc *d, const void *o, const void *w0,
+                     const void *w1, const float *bias0, const float *bias1, const float *gate0,
+                     const float *gate1, float *hidden) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!d || !o || !w0 || !hidden) return fail(ctx, LLMR_EINVAL, "null argument");
+  const long long B = d->batch, S = d->seq_len, K = d->in_dim, N = d->out_dim;
+  if (B < 1 || S < 1 || K < 64 || N < 256) return fail(ctx, LLMR_EINVAL, "empty problem");
+  if (K % 64 || N % 256)
+    return fail(ctx, LLMR_EINVAL, "in_dim must be a multiple of 64 and out_dim of 256");
+  if (d->dtype != LLMR_F16 && d->dtype != LLMR_BF16)
+    return fail(ctx, LLMR_EINVAL, "o and the weights must be fp16 or bf16");
+  const bool split = d->split_row > 0 && d->split_row < d->seq_len;
+  if (d->split_row >= d->seq_len && d->split_row > 0)
+    return fail(ctx, LLMR_EINVAL, "split_row must be below seq_len");
+  if (split && !w1) return fail(ctx, LLMR_EINVAL, "split_row > 0 needs w1");
+  auto a16 = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  const long long h_rs = d->hidden_row_stride ? (long long)d->hidden_row_stride : N;
+  if (!a16(hidden) || (h_rs % 4) || (bias0 && !a16(bias0)) || (bias1 && !a16(bias1)) ||
+      (gate0 && !a16(gate0)) || (gate1 && !a16(gate1)))
+    return fail(ctx, LLMR_EINVAL, "hidden (and its row stride), biases and gates must be 16-byte aligned");
+  if (B * S > 0x7fffffffLL) return fail(ctx, LLMR_EINVAL, "problem too large");
+  const long long o_rs = d->o_row_stride ? (long long)d->o_row_stride : K;
+  ProjParams p;
+  p.M = (int)(B * S);
+  p.S = (int)S;
+  p.B = (int)B;
+  p.split = split ? (int)d->split_row : (int)S;
+  p.seg_tiles0 = (p.split + 127) / 128;
+  p.seg_tiles1 = split ? (int)((S - p.split + 127) / 128) : 0;
+  p.k_blocks = (int)(K / 64);
+  p.n_tiles = (int)(N / 256);
+  p.tiles = p.B * (p.seg_tiles0 + p.seg_tiles1) * p.n_tiles;
+  p.out_dim = (int)N;
+  p.h_stride = h_rs;
+  p.bias[0] = bias0;
+  p.bias[1] = split ? bias1 : bias0;
+  p.gate[0] = gate0;
+  p.gate[1] = split ? gate1 : gate0;
+  p.hidden = hidden;
+  p.err = ctx->d_err;
+  CUtensorMap mx, mw0, mw1;
+  if ((rc = make_map2d(ctx, &mx, o, K, B * S, o_rs, 128))) return rc;
+  if ((rc = make_map2d(ctx, &mw0, w0, K, N, K, 256))) return rc;
+  if ((rc = make_map2d(ctx, &mw1, split ? w1 : w0, K, N, K, 256))) return rc;
+  return d->dtype == LLMR_BF16 ? launch_out_proj<true>(ctx, mx, mw0, mw1, p)
+                               : launch_out_proj<false>(ctx, mx, mw0, mw1, p);
 }
 
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {

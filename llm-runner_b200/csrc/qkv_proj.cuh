@@ -297,3 +297,231 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 }  // namespace llmr
+
+namespace llmr {
+
+// ---------------------------------------------------------------------------
+// Output projection with the gated residual in its epilogue:
+//
+//   hidden[b*S + s, n] += gate_g[n] * ( O[b*S + s, :] . W_g[n, :] + bias_g[n] )
+//
+// g = 1 for tokens s >= split_row (when split_row > 0), else 0: the joint
+// blocks' two streams (txt / img, or img / txt) with their own weights,
+// biases and gates (dependencies/flux.c3l/flux_dit.c3:874-885,
+// dependencies/qwen_edit.c3l/mmdit.c3:694-720: matmul, broadcast_bias_add
+// vit.slang:133-137, gated_residual_add vit.slang:638-647). O is the
+// attention output [B*S][in_dim] (fp16 / bf16), W_g [out_dim][in_dim] of the
+// same type, hidden fp32 [B*S][out_dim] updated in place. Same CTA layout as
+// qkv_proj_kernel; m-tiles never straddle a segment, so every tile uses one
+// weight matrix (rows of a tile beyond its segment are computed and dropped).
+struct ProjParams {
+  int M, S, B;
+  int split;             // token index where set 1 starts (S when no split)
+  int seg_tiles0;        // m-tiles of segment 0 per batch element
+  int seg_tiles1;        // m-tiles of segment 1 per batch element
+  int k_blocks;          // in_dim / 64
+  int n_tiles;           // out_dim / 256
+  int tiles;             // B * (seg_tiles0 + seg_tiles1) * n_tiles
+  int out_dim;
+  long long h_stride;    // hidden row stride (elements)
+  const float *bias[2], *gate[2];
+  float *hidden;
+  int *err;
+};
+
+// Epilogue staging: 4 warps x 32 rows x 33 floats after the pipeline's
+// barriers (16-byte aligned).
+constexpr int kProjStageOff =
+    ((QkvCfg<128, 256>::BAR_OFF + QkvCfg<128, 256>::NBAR * 8 + 16 + 15) / 16) * 16;
+constexpr int kProjSmemBytes = kProjStageOff + 4 * 32 * 33 * 4 + 1024;
+
+template <bool BF16>
+__global__ void __launch_bounds__(192, 1)
+    out_proj_kernel(const __grid_constant__ CUtensorMap tmX,
+                    const __grid_constant__ CUtensorMap tmW0,
+                    const __grid_constant__ CUtensorMap tmW1, const ProjParams p) {
+  constexpr int BN = 256;
+  using C = QkvCfg<128, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+  uint64_t *full = bars;
+  uint64_t *empty = full + C::NST;
+  uint64_t *acc_full = empty + C::NST;
+  uint64_t *acc_empty = acc_full + 2;
+  uint64_t *drain = acc_empty + 2;
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int mt_per_b = p.seg_tiles0 + p.seg_tiles1;
+  const int m_tiles = p.B * mt_per_b;
+  // Tile -> (first row, last row + 1 of its segment, weight set, column).
+  // Groups of 16 m-tiles walked m-fastest over all column blocks (L2 reuse).
+  constexpr int kGroupM = 16;
+  auto decode = [&](int tile, int &m0, int &m_end, int &set, int &n0) {
+    const int per_group = kGroupM * p.n_tiles;
+    const int grp = tile / per_group;
+    const int first = grp * kGroupM;
+    const int gm = m_tiles - first < kGroupM ? m_tiles - first : kGroupM;
+    const int in = tile - grp * per_group;
+    const int mt = first + in % gm;
+    n0 = (in / gm) * BN;
+    const int b = mt / mt_per_b, r = mt - b * mt_per_b;
+    set = r < p.seg_tiles0 ? 0 : 1;
+    const int seg0 = set == 0 ? 0 : p.split;
+    const int seg1 = set == 0 ? p.split : p.S;
+    m0 = b * p.S + seg0 + (set == 0 ? r : r - p.seg_tiles0) * C::BM;
+    m_end = b * p.S + seg1;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::NST; i++) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_base_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      tma_prefetch_desc(&tmW0);
+      tma_prefetch_desc(&tmW1);
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x) {
+        int m0, m_end, set, n0;
+        decode(tile, m0, m_end, set, n0);
+        const CUtensorMap *mw = set ? &tmW1 : &tmW0;
+        for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+          const int st = it % C::NST, round = it / C::NST;
+          if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sa = smem + st * C::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[st], C::STAGE_BYTES);
+          tma_load_2d(sa, &tmX, &full[st], kb * C::BK, m0);
+          tma_load_2d(sa + C::A_BYTES, mw, &full[st], kb * C::BK, n0);
+        }
+      }
+      if (!ok) {
+        for (int u = it - C::NST < 0 ? 0 : it - C::NST; u < it; u++)
+          mbar_wait_raw(&full[u % C::NST], (u / C::NST) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    constexpr uint32_t IDESC = idesc_mma_f32(C::BM, BN, BF16 ? 1u : 0u);
+    const uint32_t sbase = smem_u32(smem);
+    bool ok = true;
+    int it = 0;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, local++) {
+      const int buf = local & 1;
+      if (local >= 2 && !(ok = mbar_wait(&acc_empty[buf], ((local >> 1) - 1) & 1, abort_flag)))
+        break;
+      tc_fence_after();
+      for (int kb = 0; kb < p.k_blocks; kb++, it++) {
+        const int st = it % C::NST;
+        if (!(ok = mbar_wait(&full[st], (it / C::NST) & 1, abort_flag))) break;
+        tc_fence_after();
+        const uint32_t a = sbase + st * C::STAGE_BYTES;
+        const uint32_t b = a + C::A_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < C::BK / 16; kk++) {
+          if (elect_one())
+            mma_ss(tmem + buf * BN, sdesc_sw128(a + kk * 32, 16, 1024),
+                   sdesc_sw128(b + kk * 32, 16, 1024), IDESC, (kb > 0 || kk > 0) ? 1u : 0u);
+        }
+        if (elect_one()) mma_commit(&empty[st]);
+      }
+      if (!ok) break;
+      if (elect_one()) mma_commit(&acc_full[buf]);
+    }
+    if (elect_one()) mma_commit(drain);
+    mbar_wait_raw(drain, 0, 100000000ull);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    // Per 32-column chunk: each thread (one accumulator row) parks its 32
+    // values in this warp's padded staging block; the warp then updates the
+    // 32 rows one at a time with coalesced 128-byte accesses, all 32 rows'
+    // loads of `hidden` issued before any store.
+    const int quarter = warp & 3;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float *stage = reinterpret_cast<float *>(smem + kProjStageOff) + (warp - 2) * 32 * 33;
+    bool ok = true;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.tiles && ok; tile += gridDim.x, local++) {
+      const int buf = local & 1;
+      int m0, m_end, set, n0;
+      decode(tile, m0, m_end, set, n0);
+      ok = __all_sync(0xffffffffu, mbar_wait(&acc_full[buf], (local >> 1) & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      // select by value: indexing the parameter arrays would copy them to
+      // local memory
+      const float *bias = set ? p.bias[1] : p.bias[0];
+      const float *gate = set ? p.gate[1] : p.gate[0];
+      const int rbase = m0 + quarter * 32;      // first row of this warp
+      const int rlim = m_end < p.M ? m_end : p.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; c++) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + buf * BN + c * 32, r);
+        tmem_wait_ld();
+        reg_fence32(r);
+        if (c == BN / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+#pragma unroll
+        for (int k = 0; k < 32; k++) stage[lane * 33 + k] = __uint_as_float(r[k]);
+        __syncwarp();
+        const int col = n0 + c * 32 + lane;
+        const float bj = bias != nullptr ? bias[col] : 0.0f;
+        const float gj = gate != nullptr ? gate[col] : 1.0f;
+        float hv[32];
+#pragma unroll
+        for (int rr = 0; rr < 32; rr++)
+          hv[rr] = rbase + rr < rlim ? p.hidden[(long long)(rbase + rr) * p.h_stride + col] : 0.0f;
+#pragma unroll
+        for (int rr = 0; rr < 32; rr++)
+          if (rbase + rr < rlim)
+            p.hidden[(long long)(rbase + rr) * p.h_stride + col] =
+                hv[rr] + gj * (stage[rr * 33 + lane] + bj);
+        __syncwarp();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
+}
+
+}  // namespace llmr

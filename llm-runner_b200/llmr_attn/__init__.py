@@ -81,6 +81,16 @@ class QkvDesc(ctypes.Structure):
     ]
 
 
+class ProjDesc(ctypes.Structure):
+    """llmr_proj_desc (include/llmr_attn.h)."""
+    _fields_ = [
+        ("batch", ctypes.c_uint32), ("seq_len", ctypes.c_uint32),
+        ("in_dim", ctypes.c_uint32), ("out_dim", ctypes.c_uint32),
+        ("dtype", ctypes.c_int), ("split_row", ctypes.c_uint32),
+        ("o_row_stride", ctypes.c_uint64), ("hidden_row_stride", ctypes.c_uint64),
+    ]
+
+
 class IpcHandle(ctypes.Structure):
     """llmr_ipc_handle: an exported device allocation (64 opaque bytes)."""
     _fields_ = [("bytes", ctypes.c_ubyte * 64)]
@@ -128,6 +138,8 @@ def _load() -> ctypes.CDLL:
                                                vp, vp, vp, vp, vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
         "llmr_qkv_project": (i32, [vp, ctypes.POINTER(QkvDesc), vp, vp, vp, vp, vp, vp, vp]),
+        "llmr_out_project": (i32, [vp, ctypes.POINTER(ProjDesc), vp, vp, vp, vp, vp, vp, vp,
+                                   vp]),
         "llmr_ipc_export": (i32, [vp, vp, ctypes.POINTER(IpcHandle)]),
         "llmr_ipc_open": (i32, [vp, ctypes.POINTER(IpcHandle), ctypes.POINTER(vp)]),
         "llmr_ipc_close": (i32, [vp, vp]),
@@ -410,6 +422,26 @@ def qkv_project(ctx: Context, x, w, qkv_out, cfg: AttnConfig, *, batch: int, seq
                                    _ptr(qkv_out)))
 
 
+def out_project(ctx: Context, o, hidden, w0, w1=None, *, batch: int, seq_len: int,
+                split_row: int = 0, bias0=None, bias1=None, gate0=None, gate1=None) -> None:
+    """hidden (fp32 [B*S, out_dim]) += gate_g * (o . w_g^T + bias_g), weight
+    set g = 1 for tokens >= split_row (when split_row > 0). o [B*S, in_dim]
+    and the weights [out_dim, in_dim] are both fp16 or both bf16."""
+    d = ProjDesc()
+    d.batch, d.seq_len = batch, seq_len
+    d.in_dim, d.out_dim = o.shape[-1], w0.shape[0]
+    d.dtype = _dtype_code(o)
+    d.split_row = split_row
+    d.o_row_stride = o.stride(-2)
+    d.hidden_row_stride = hidden.stride(-2)
+    for w in (w0, w1):
+        if w is not None and _dtype_code(w) != d.dtype:
+            raise LlmrError(EINVAL, "o and the weights must have the same dtype")
+    ctx.check(lib.llmr_out_project(ctx.handle, ctypes.byref(d), _ptr(o), _ptr(w0), _ptr(w1),
+                                   _ptr(bias0), _ptr(bias1), _ptr(gate0), _ptr(gate1),
+                                   _ptr(hidden)))
+
+
 # --------------------------------------------------------------------- peer buffers
 
 _TYPESTR = {"float16": "<f2", "bfloat16": None, "float32": "<f4", "uint8": "|u1"}
@@ -516,6 +548,6 @@ __all__ = [
     "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
     "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
     "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
-    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "qkv_project", "QkvDesc", "IpcHandle", "LIB_PATH",
+    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "qkv_project", "QkvDesc", "out_project", "ProjDesc", "IpcHandle", "LIB_PATH",
     "lib",
 ]

@@ -34,6 +34,7 @@ def test_library_exports_every_declared_symbol():
 
 @pytest.mark.parametrize("py_name,c_name", [("AttnDesc", "llmr_attn_desc"),
                                              ("QkvDesc", "llmr_qkv_desc"),
+                                             ("ProjDesc", "llmr_proj_desc"),
                                              ("IpcHandle", "llmr_ipc_handle")])
 def test_desc_layout_matches_c(py_name, c_name):
     """The ctypes structs have the C structs' sizes and field offsets."""

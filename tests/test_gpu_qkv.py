@@ -134,3 +134,57 @@ def test_qkv_project_rejects_bad_shapes(ctx):
     w16 = torch.zeros((3 * 128, 128), device="cuda", dtype=torch.float16)
     with pytest.raises(L.LlmrError):
         L.qkv_project(ctx, xb, w16, out, cfg, batch=1, seq_len=64)   # mixed dtypes
+
+
+# ------------------------------------------------------------------ out projection
+
+@pytest.mark.parametrize("B,S,in_dim,out_dim,split,dtype,with_bias,with_gate", [
+    (1, 300, 256, 512, 100, "f16", True, True),     # two streams, ragged segments
+    (2, 257, 192, 256, 0, "bf16", False, True),     # one stream, bf16, batch 2
+    (1, 128, 64, 768, 64, "bf16", True, False),     # one k block, three column tiles
+])
+def test_out_project_vs_numpy(ctx, B, S, in_dim, out_dim, split, dtype, with_bias, with_gate):
+    """hidden += gate_g * (o . w_g^T + bias_g), g by token index: the
+    reference's matmul + broadcast_bias_add + gated_residual_add per stream."""
+    import llmr_attn as L
+    torch = _t()
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    g = torch.Generator().manual_seed(S + out_dim)
+    o = torch.randn((B * S, in_dim), generator=g).to(tdt)
+    w = [(torch.randn((out_dim, in_dim), generator=g) * in_dim ** -0.5).to(tdt) for _ in range(2)]
+    bias = [torch.randn(out_dim, generator=g) if with_bias else None for _ in range(2)]
+    gate = [torch.rand(out_dim, generator=g) + 0.5 if with_gate else None for _ in range(2)]
+    hidden = torch.randn((B * S, out_dim), generator=g)
+    want = hidden.double().clone()
+    for b in range(B):
+        for s0, s1, k in ((0, split if split else S, 0), (split, S, 1)) if split else ((0, S, 0),):
+            rows = slice(b * S + s0, b * S + s1)
+            y = o[rows].double() @ w[k].double().t()
+            if bias[k] is not None:
+                y = y + bias[k].double()
+            if gate[k] is not None:
+                y = y * gate[k].double()
+            want[rows] += y
+    cu = lambda t: None if t is None else t.cuda()
+    hd = hidden.cuda()
+    L.out_project(ctx, o.cuda(), hd, cu(w[0]), cu(w[1]) if split else None, batch=B, seq_len=S,
+                  split_row=split, bias0=cu(bias[0]), bias1=cu(bias[1]), gate0=cu(gate[0]),
+                  gate1=cu(gate[1]))
+    ctx.sync()
+    err = (hd.cpu().double() - want).abs()
+    assert err.max().item() < 2e-4 * max(1.0, want.abs().max().item()), err.max().item()
+
+
+def test_out_project_rejects_bad_shapes(ctx):
+    import llmr_attn as L
+    torch = _t()
+    o = torch.zeros((64, 128), device="cuda", dtype=torch.float16)
+    w = torch.zeros((200, 128), device="cuda", dtype=torch.float16)     # out_dim % 256
+    h = torch.zeros((64, 200), device="cuda")
+    with pytest.raises(L.LlmrError) as ei:
+        L.out_project(ctx, o, h, w, batch=1, seq_len=64)
+    assert ei.value.status == L.EINVAL
+    w2 = torch.zeros((256, 128), device="cuda", dtype=torch.float16)
+    h2 = torch.zeros((64, 256), device="cuda")
+    with pytest.raises(L.LlmrError):        # a split without the second weight set
+        L.out_project(ctx, o, h2, w2, batch=1, seq_len=64, split_row=32)
