@@ -60,6 +60,10 @@ def parse():
                     help="the output projection with the gated residual in its epilogue "
                          "(llmr_out_project, txt/img weight sets) against cuBLAS GEMMs per "
                          "stream followed by torch's bias / gate / residual ops")
+    ap.add_argument("--varlen", action="store_true",
+                    help="the CFG pair with different text lengths (Z-Image shapes: 256 + 4096 "
+                         "and 0 + 4096 tokens, H30 D128 bf16, norm + RoPE) as one packed "
+                         "llmr_attention_varlen call against two llmr_attention_fused calls")
     ap.add_argument("--cpu-table", action="store_true",
                     help="only the CPU baseline: the oracle on all host cores and on 1 core, "
                          "every configuration, a bounded row sample each")
@@ -312,6 +316,69 @@ def proj_bench(args):
     ctx.close()
 
 
+def varlen_bench(args):
+    """Packed cond/uncond sequences (4352 and 4096 tokens) in one launch pair
+    (prologue + attention) against one fused call per sequence."""
+    import numpy as np
+    import torch
+
+    import llmr_attn as L
+    H, D = 30, 128
+    lens = (4352, 4096)
+    T = sum(lens)
+    g = torch.Generator(device="cuda").manual_seed(3)
+    q, k, v = (torch.randn((1, T, H, D), device="cuda", generator=g).bfloat16()
+               for _ in range(3))
+    gain = torch.ones(D, device="cuda")
+    tabs = []
+    for i, n in enumerate(lens):
+        pos = np.stack([np.full(n, i), np.arange(n) // 64, np.arange(n) % 64], 1).astype(np.int32)
+        tabs.append(L.rope_tables(pos, (32, 48, 48), 256.0))
+    cos = torch.from_numpy(np.concatenate([c for c, _ in tabs])).cuda()
+    sin = torch.from_numpy(np.concatenate([s_ for _, s_ in tabs])).cuda()
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=D ** -0.5, norm_q=True, norm_k=True,
+                       rope=True, eps=1e-5)
+    o = torch.empty((1, T, H * D), device="cuda", dtype=torch.bfloat16)
+    ctx = L.Context(0)
+    ctx.reserve(3 * T * H * D * 2)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def packed():
+        L.attention_varlen(ctx, q, k, v, o, cfg, lens, q_gain=gain, k_gain=gain, cos=cos,
+                           sin=sin)
+
+    def separate():
+        off = 0
+        for n in lens:
+            sl = slice(off, off + n)
+            L.attention_fused(ctx, q[:, sl], k[:, sl], v[:, sl], o[:, sl], cfg, batch=1,
+                              seq_len=n, q_gain=gain, k_gain=gain, cos=cos[sl], sin=sin[sl])
+            off += n
+
+    res = {}
+    for name, fn in (("packed", packed), ("separate", separate)):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        res[name] = sum(ts) / len(ts)
+    flops = sum(4.0 * H * n * n * D for n in lens)
+    print(json.dumps({"varlen": "zimage_cfg_pair", "seq_lens": lens, "n_heads": H,
+                      "packed_ms": res["packed"], "separate_ms": res["separate"],
+                      "packed_tflops": flops / (res["packed"] / 1e3) / 1e12,
+                      "speedup": res["separate"] / res["packed"], "steps": args.steps}),
+          flush=True)
+    ctx.close()
+
+
 def cpu_table(args):
     """The oracle per configuration on all host cores and on one core, each
     over a row sample of about 8 s, extrapolated to the whole op."""
@@ -515,6 +582,9 @@ def main():
         return
     if args.proj:
         proj_bench(args)
+        return
+    if args.varlen:
+        varlen_bench(args)
         return
     if args.profile_run:
         profile_run(args)

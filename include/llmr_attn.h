@@ -298,6 +298,22 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *desc,
                          const float *cos_t, const float *sin_t, void *o,
                          float *lse);
 
+/* Variable-length batch: q/k/v hold n_seqs sequences back to back as one
+ * batch element of desc->seq_len = sum(seq_lens) tokens (desc->batch must be
+ * 1; any layout and strides of llmr_attention_fused), and each sequence
+ * attends only within itself — e.g. the cond/uncond pair of a CFG step with
+ * different text lengths, which the reference runs as two forwards
+ * (dependencies/zimage.c3l/pipeline.c3:494-520), in one call. The RoPE row of
+ * packed token t is rope_row_offset + t (concatenate the sequences' tables).
+ * split_row must be 0; LLMR_EXACT, LLMR_MERGE and kv_seq_len are not
+ * supported. seq_lens: host array, 1 <= n_seqs <= 64. */
+int llmr_attention_varlen(llmr_ctx *ctx, const llmr_attn_desc *desc,
+                          const uint32_t *seq_lens, uint32_t n_seqs,
+                          const void *q, const void *k, const void *v,
+                          const float *q_gain, const float *k_gain,
+                          const float *cos_t, const float *sin_t, void *o,
+                          float *lse);
+
 /* Allocation-free variant of llmr_attention_fused (tensor-core path only).
  * It has no counterpart in the reference. It is for callers that cannot
  * allocate device memory: those whose HBM belongs to another allocator (a

@@ -29,12 +29,20 @@
 
 namespace llmr {
 
+constexpr int kMaxSeqs = 64;  // packed sequences of one variable-length call
+
 struct FaParams {
-  int S;                 // queries per (b, h)
+  int S;                 // queries per (b, h) (packed: total tokens)
   int S_kv;              // keys per (b, h)
   int H;                 // heads
   int nqt;               // query-tile pairs (256 queries) per (b, h)
-  int units;             // B * H * nqt work units
+  int units;             // work units (B * H * nqt, or the packed total)
+  // Variable-length mode (nseq > 0): the maps hold one packed batch element
+  // of S tokens; sequence i is tokens [seq_off[i], seq_off[i+1]) and owns
+  // units [unit_off[i], unit_off[i+1]) (H * its query-tile pairs).
+  int nseq;
+  int seq_off[kMaxSeqs + 1];
+  int unit_off[kMaxSeqs + 1];
   float scale_log2;      // softmax scale * log2(e)
   void *o;               // output base (OutT)
   long long o_row_stride;    // elements between consecutive tokens
@@ -79,7 +87,16 @@ template <int D>
 inline dim3 fa_grid(FaParams &p, int B, int num_sms) {
   using C = FaCfg<D>;
   p.nqt = (p.S + 2 * C::BM - 1) / (2 * C::BM);
-  p.units = B * p.H * p.nqt;
+  if (p.nseq > 0) {
+    p.unit_off[0] = 0;
+    for (int i = 0; i < p.nseq; i++) {
+      const int len = p.seq_off[i + 1] - p.seq_off[i];
+      p.unit_off[i + 1] = p.unit_off[i] + p.H * ((len + 2 * C::BM - 1) / (2 * C::BM));
+    }
+    p.units = p.unit_off[p.nseq];
+  } else {
+    p.units = B * p.H * p.nqt;
+  }
   const int sms = num_sms > 0 ? num_sms : 148;
   return dim3(p.units < sms ? p.units : sms);
 }
@@ -172,15 +189,40 @@ __global__ void __launch_bounds__(384, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int S = p.S;
-  const int nblk = (p.S_kv + C::BN - 1) / C::BN;  // key blocks per unit
   // Work units (b, h, query-tile pair), persistent over the grid: this CTA
   // takes units blockIdx.x, blockIdx.x + gridDim.x, ... Consecutive units
-  // share (b, h), so CTAs running together share K/V tiles in L2.
-  auto decode = [&](int unit, int &b, int &h, int &q0) {
-    const int bh = unit / p.nqt;
-    q0 = (unit - bh * p.nqt) * 2 * C::BM;
-    b = bh / p.H;
-    h = bh - b * p.H;
+  // share (b, h), so CTAs running together share K/V tiles in L2. A unit's
+  // geometry: map batch coordinate b, head h, first query q0 (relative to
+  // row0, the first token of its sequence in the maps), its query and key
+  // counts, and its number of key blocks.
+  struct Unit {
+    int b, h, q0, row0, sq, sk, nblk;
+  };
+  auto decode = [&](int unit) {
+    Unit u;
+    if (p.nseq > 0) {
+      int i = 0;
+      while (i + 1 < p.nseq && unit >= p.unit_off[i + 1]) i++;
+      const int len = p.seq_off[i + 1] - p.seq_off[i];
+      const int nqt = (len + 2 * C::BM - 1) / (2 * C::BM);
+      const int local = unit - p.unit_off[i];
+      u.h = local / nqt;
+      u.q0 = (local - u.h * nqt) * 2 * C::BM;
+      u.b = 0;
+      u.row0 = p.seq_off[i];
+      u.sq = len;
+      u.sk = len;
+    } else {
+      const int bh = unit / p.nqt;
+      u.q0 = (unit - bh * p.nqt) * 2 * C::BM;
+      u.b = bh / p.H;
+      u.h = bh - u.b * p.H;
+      u.row0 = 0;
+      u.sq = p.S;
+      u.sk = p.S_kv;
+    }
+    u.nblk = (u.sk + C::BN - 1) / C::BN;
+    return u;
   };
 
   if (threadIdx.x == 0) {
@@ -221,9 +263,10 @@ __global__ void __launch_bounds__(384, 1)
         bool ok = true;
         int issued = 0;  // K/V tile loads armed so far (over all units)
         int kq = 0;      // Q loads armed so far
+        int jb = 0;      // key blocks of this CTA's earlier units
         for (int unit = blockIdx.x, k = 0; unit < p.units && ok; unit += gridDim.x, k++) {
-          int b, h, q0;
-          decode(unit, b, h, q0);
+          const Unit un = decode(unit);
+          const int b = un.b, h = un.h, nblk = un.nblk;
           // Q of this unit may replace the previous unit's once its last
           // S MMAs have completed.
           if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, abort_flag)) {
@@ -234,11 +277,11 @@ __global__ void __launch_bounds__(384, 1)
           for (int t = 0; t < 2; t++)
             for (int c = 0; c < C::NCHUNK; c++)
               tma_load_4d(sQ + t * C::TILE_BYTES + c * C::CHUNK_BYTES, &tmQ, q_full,
-                          c * 64, q0 + t * C::BM, h, b);
+                          c * 64, un.row0 + un.q0 + t * C::BM, h, b);
           kq = k + 1;
           for (int j = 0; j < nblk && ok; j++) {
             for (int kind = 0; kind < 2; kind++) {
-              const int u = 2 * (k * nblk + j) + kind;
+              const int u = 2 * (jb + j) + kind;
               const int slot = u % C::NST, round = u / C::NST;
               if (round > 0 && !mbar_wait(&kv_empty[slot], (round - 1) & 1, abort_flag)) {
                 ok = false;
@@ -248,10 +291,11 @@ __global__ void __launch_bounds__(384, 1)
               const CUtensorMap *m = kind ? &tmV : &tmK;
               for (int c = 0; c < C::NCHUNK; c++)
                 tma_load_4d(sKV + slot * C::TILE_BYTES + c * C::CHUNK_BYTES, m,
-                            &kv_full[slot], c * 64, j * C::BN, h, b);
+                            &kv_full[slot], c * 64, un.row0 + j * C::BN, h, b);
               issued = u + 1;
             }
           }
+          jb += nblk;
         }
         if (!ok) {
           // Abort path: let every armed copy land before the CTA exits.
@@ -300,8 +344,10 @@ __global__ void __launch_bounds__(384, 1)
         return true;
       };
       bool ok = true;
+      int jb = 0;  // key blocks of this CTA's earlier units
       for (int unit = blockIdx.x, k = 0; unit < p.units && ok; unit += gridDim.x, k++) {
-        const int ub = 2 * k * nblk;  // K/V ring position of this unit's K_0
+        const int nblk = decode(unit).nblk;
+        const int ub = 2 * jb;  // K/V ring position of this unit's K_0
         ok = mbar_wait(q_full, k & 1, abort_flag);
         if (ok) ok = mbar_wait(&kv_full[ub % C::NST], (ub / C::NST) & 1, abort_flag);
         if (!ok) break;
@@ -315,7 +361,7 @@ __global__ void __launch_bounds__(384, 1)
         if (elect_one()) mma_commit(&kv_empty[ub % C::NST]);
         if (nblk == 1 && elect_one()) mma_commit(q_empty);
         for (int j = 0; j < nblk; j++) {
-          const int jj = k * nblk + j;
+          const int jj = jb + j;
           const int uV = 2 * jj + 1, sV = uV % C::NST;
           const int uK = 2 * jj + 2, sK = uK % C::NST;
           const bool more = j + 1 < nblk;
@@ -345,6 +391,7 @@ __global__ void __launch_bounds__(384, 1)
             if (elect_one()) mma_commit(&o_full[1]);
           }
         }
+        jb += nblk;
       }
       // Drain: every MMA this warp issued has completed before TMEM is
       // released at the end of the kernel.
@@ -361,19 +408,20 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tO = tmem + lane_off + C::O_COL + t * D;
     const float sl2 = p.scale_log2;
     bool ok = true;
+    int jb = 0;  // key blocks of this CTA's earlier units
     for (int unit = blockIdx.x, k = 0; unit < p.units && ok; unit += gridDim.x, k++) {
-      int b, h, q0;
-      decode(unit, b, h, q0);
+      const Unit un = decode(unit);
+      const int b = un.b, h = un.h, nblk = un.nblk;
       const int bh = b * p.H + h;
       float m_used = -INFINITY;  // log2-domain max the P values are relative to
       float l = 0.0f;
       for (int j = 0; j < nblk; j++) {
-        const int jj = k * nblk + j;
+        const int jj = jb + j;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], jj & 1, abort_flag));
         if (!ok) break;
         tc_fence_after();
-        const int valid = p.S_kv - j * C::BN;  // keys of this block below S_kv
-        // Applies the key mask (keys >= S_kv -> -inf) to chunk c.
+        const int valid = un.sk - j * C::BN;  // keys of this block inside the sequence
+        // Applies the key mask (keys past the sequence -> -inf) to chunk c.
         auto mask_chunk = [&](int c, float *v) {
           if (valid < C::BN) {
 #pragma unroll
@@ -456,12 +504,15 @@ __global__ void __launch_bounds__(384, 1)
         const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
         l += (s0.x + s0.y) + (s1.x + s1.y);
       }
+      jb += nblk;
       if (!ok) break;
       // ------------------------------------------------------- epilogue
       ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], k & 1, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      const int qrow = q0 + t * C::BM + row;
+      const int qloc = un.q0 + t * C::BM + row;  // query within its sequence
+      const bool qin = qloc < un.sq;
+      const int qrow = un.row0 + qloc;            // row in the maps / output
       OutT *dst = reinterpret_cast<OutT *>(p.o) + (long long)b * p.o_batch_stride +
                   (long long)qrow * p.o_row_stride + (long long)h * D;
       const float lse_t = (m_used + log2f(l)) * 0.69314718055994531f;
@@ -470,7 +521,7 @@ __global__ void __launch_bounds__(384, 1)
       // keys, read from o and lse in place) and of this one.
       float ca = 0.0f, ct = 1.0f / l, lse_out = lse_t;
       constexpr bool kCanMerge = std::is_same<OutT, float>::value;
-      const bool merge = kCanMerge && p.merge && qrow < S;
+      const bool merge = kCanMerge && p.merge && qin;
       if (merge) {
         const float la = p.lse[(long long)bh * S + qrow];
         const float mx2 = fmaxf(la, lse_t);
@@ -507,9 +558,9 @@ __global__ void __launch_bounds__(384, 1)
             }
           }
         }
-        if (qrow < S) store_row_chunk<OutT>(dst + c * 32, v);
+        if (qin) store_row_chunk<OutT>(dst + c * 32, v);
       }
-      if (p.lse != nullptr && qrow < S) p.lse[(long long)bh * S + qrow] = lse_out;
+      if (p.lse != nullptr && qin) p.lse[(long long)bh * S + qrow] = lse_out;
     }
   }
 

@@ -172,7 +172,8 @@ int launch_out_proj(llmr_ctx *ctx, const CUtensorMap &mx, const CUtensorMap &mw0
 template <int D, typename OutT>
 int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                  const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
-                 long long o_rs, long long o_bs, float *lse, int merge) {
+                 long long o_rs, long long o_bs, float *lse, int merge, int nseq,
+                 const int *seq_off) {
   using C = FaCfg<D>;
   static bool attr_set = false;
   if (!attr_set) {
@@ -199,6 +200,9 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   p.lse = lse;
   p.merge = merge;
   p.err = ctx->d_err;
+  p.nseq = seq_off != nullptr ? nseq : 0;
+  p.seq_off[0] = 0;
+  for (int i = 0; i <= p.nseq && p.nseq > 0; i++) p.seq_off[i] = seq_off[i];
   const dim3 grid = fa_grid<D>(p, B, ctx->num_sms);
   fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
   return after_launch(ctx, "fa_fwd_tc");
@@ -207,21 +211,17 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
 int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
                      const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S, int S_kv,
                      float scale, void *o, long long o_rs, long long o_bs, float *lse,
-                     int merge) {
+                     int merge, int nseq = 0, const int *seq_off = nullptr) {
+#define LLMR_FA_ARGS ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse
   if (D == 128) {
-    if (od == LLMR_F32)
-      return launch_fa_tc<128, float>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, merge);
-    if (od == LLMR_F16)
-      return launch_fa_tc<128, __half>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, 0);
-    return launch_fa_tc<128, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs,
-                                            lse, 0);
+    if (od == LLMR_F32) return launch_fa_tc<128, float>(LLMR_FA_ARGS, merge, nseq, seq_off);
+    if (od == LLMR_F16) return launch_fa_tc<128, __half>(LLMR_FA_ARGS, 0, nseq, seq_off);
+    return launch_fa_tc<128, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off);
   }
-  if (od == LLMR_F32)
-    return launch_fa_tc<64, float>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, merge);
-  if (od == LLMR_F16)
-    return launch_fa_tc<64, __half>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse, 0);
-  return launch_fa_tc<64, __nv_bfloat16>(ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse,
-                                         0);
+  if (od == LLMR_F32) return launch_fa_tc<64, float>(LLMR_FA_ARGS, merge, nseq, seq_off);
+  if (od == LLMR_F16) return launch_fa_tc<64, __half>(LLMR_FA_ARGS, 0, nseq, seq_off);
+  return launch_fa_tc<64, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off);
+#undef LLMR_FA_ARGS
 }
 
 template <int D, typename InT, typename OutT>
@@ -619,9 +619,47 @@ size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {
   return 3 * n * 2;
 }
 
+static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, const void *k,
+                          const void *v, const float *q_gain, const float *k_gain,
+                          const float *cos_t, const float *sin_t, void *o, float *lse,
+                          int nseq, const int *seq_off);
+
 int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, const void *k,
                          const void *v, const float *q_gain, const float *k_gain,
                          const float *cos_t, const float *sin_t, void *o, float *lse) {
+  return attention_core(ctx, d, q, k, v, q_gain, k_gain, cos_t, sin_t, o, lse, 0, nullptr);
+}
+
+int llmr_attention_varlen(llmr_ctx *ctx, const llmr_attn_desc *d, const uint32_t *seq_lens,
+                          uint32_t n_seqs, const void *q, const void *k, const void *v,
+                          const float *q_gain, const float *k_gain, const float *cos_t,
+                          const float *sin_t, void *o, float *lse) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  if (!d || !seq_lens) return fail(ctx, LLMR_EINVAL, "null argument");
+  if (n_seqs < 1 || n_seqs > (uint32_t)kMaxSeqs)
+    return fail(ctx, LLMR_EINVAL, "n_seqs must be in [1, %d]", kMaxSeqs);
+  if (d->batch != 1) return fail(ctx, LLMR_EINVAL, "packed sequences: batch must be 1");
+  if (d->split_row != 0) return fail(ctx, LLMR_EINVAL, "varlen: split_row must be 0");
+  if (d->flags & (LLMR_EXACT | LLMR_MERGE))
+    return fail(ctx, LLMR_EINVAL, "varlen: LLMR_EXACT and LLMR_MERGE are not supported");
+  if (d->kv_seq_len != 0 && d->kv_seq_len != d->seq_len)
+    return fail(ctx, LLMR_EINVAL, "varlen: kv_seq_len must be 0");
+  int off[kMaxSeqs + 1];
+  off[0] = 0;
+  for (uint32_t i = 0; i < n_seqs; i++) {
+    if (seq_lens[i] < 1) return fail(ctx, LLMR_EINVAL, "sequence %u is empty", i);
+    off[i + 1] = off[i] + (int)seq_lens[i];
+  }
+  if ((uint32_t)off[n_seqs] != d->seq_len)
+    return fail(ctx, LLMR_EINVAL, "seq_lens sum to %d, seq_len is %u", off[n_seqs], d->seq_len);
+  return attention_core(ctx, d, q, k, v, q_gain, k_gain, cos_t, sin_t, o, lse, (int)n_seqs, off);
+}
+
+static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, const void *k,
+                          const void *v, const float *q_gain, const float *k_gain,
+                          const float *cos_t, const float *sin_t, void *o, float *lse,
+                          int nseq, const int *seq_off) {
   int rc = check_ctx(ctx);
   if (rc) return rc;
   if (!d || !q || !k || !v || !o) return fail(ctx, LLMR_EINVAL, "null argument");
@@ -717,7 +755,7 @@ int llmr_attention_fused(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q, 
   }
   mark(1);
   rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
-                        o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0);
+                        o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0, nseq, seq_off);
   mark(2);
   ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
   return rc;

@@ -171,6 +171,8 @@ int attention(cudaStream_t st, int num_sms, const CUtensorMap &mq, const CUtenso
   p.lse = lse;
   p.merge = 0;
   p.err = err;
+  p.nseq = 0;
+  p.seq_off[0] = 0;
   const dim3 grid = fa_grid<D>(p, B, num_sms);
   fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(mq, mk, mv, p);
   return cudaGetLastError() == cudaSuccess ? LLMR_OK : LLMR_ECUDA;

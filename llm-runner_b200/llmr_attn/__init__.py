@@ -138,6 +138,8 @@ def _load() -> ctypes.CDLL:
                                                vp, vp, vp, vp, vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
         "llmr_qkv_project": (i32, [vp, ctypes.POINTER(QkvDesc), vp, vp, vp, vp, vp, vp, vp]),
+        "llmr_attention_varlen": (i32, [vp, ctypes.POINTER(AttnDesc), vp, u32, vp, vp, vp, vp,
+                                        vp, vp, vp, vp, vp]),
         "llmr_out_project": (i32, [vp, ctypes.POINTER(ProjDesc), vp, vp, vp, vp, vp, vp, vp,
                                    vp]),
         "llmr_ipc_export": (i32, [vp, vp, ctypes.POINTER(IpcHandle)]),
@@ -351,6 +353,24 @@ def attention_fused(ctx: Context, q, k, v, o, cfg: AttnConfig, *, batch: int, se
                                        _ptr(sin), _ptr(o), _ptr(lse)))
 
 
+def attention_varlen(ctx: Context, q, k, v, o, cfg: AttnConfig, seq_lens, *, q_gain=None,
+                     k_gain=None, cos=None, sin=None, lse=None,
+                     strides: Optional[dict] = None) -> None:
+    """Packed variable-length sequences (llmr_attention_varlen): q/k/v/o hold
+    len(seq_lens) sequences back to back as one batch element of
+    sum(seq_lens) tokens; each attends within itself. cos/sin rows follow the
+    packed token index (concatenated tables); no txt/img split."""
+    lens = (ctypes.c_uint32 * len(seq_lens))(*[int(x) for x in seq_lens])
+    tokens = q.shape[-3] if cfg.layout == BSHD else q.shape[-2]
+    if tokens != int(sum(seq_lens)):
+        raise LlmrError(EINVAL, f"seq_lens sum to {int(sum(seq_lens))}, q holds {tokens} tokens")
+    desc = make_desc(cfg, 1, int(sum(seq_lens)), _dtype_code(q), _dtype_code(o),
+                     lse=lse is not None, strides=strides)
+    ctx.check(lib.llmr_attention_varlen(ctx.handle, ctypes.byref(desc), lens, len(seq_lens),
+                                        _ptr(q), _ptr(k), _ptr(v), _ptr(q_gain), _ptr(k_gain),
+                                        _ptr(cos), _ptr(sin), _ptr(o), _ptr(lse)))
+
+
 NOALLOC_SCRATCH_BYTES = 64 << 20
 
 
@@ -548,6 +568,6 @@ __all__ = [
     "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
     "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
     "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
-    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "qkv_project", "QkvDesc", "out_project", "ProjDesc", "IpcHandle", "LIB_PATH",
+    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "qkv_project", "QkvDesc", "out_project", "ProjDesc", "attention_varlen", "IpcHandle", "LIB_PATH",
     "lib",
 ]

@@ -500,3 +500,61 @@ def test_bounded_wait_timeout_is_reported(ctx):
     check(host(o), oracle_fa(q, q, q, 0.125).reshape(1, 100, 128), what="after timeout")
     with pytest.raises(L.LlmrError):
         ctx.check(L.lib.llmr_selftest_wait_timeout(ctx.handle, 0))
+
+
+# -------------------------------------------------------------- variable length
+
+@pytest.mark.parametrize("D,lens", [(128, (300, 129, 1000)), (64, (17, 640)),
+                                    (128, (4352, 4096))])
+def test_varlen_packed_sequences(ctx, D, lens):
+    """llmr_attention_varlen: packed sequences of different lengths (the CFG
+    pair with different text lengths is the last case) each equal the
+    oracle's block on that sequence alone, with QK-RMSNorm and per-sequence
+    RoPE tables concatenated in packing order."""
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(sum(lens) + D)
+    H, T = 3, sum(lens)
+    q, k, v = (rng.standard_normal((T, H, D), dtype=np.float32) for _ in range(3))
+    q, k, v = (a.astype(np.float16).astype(np.float32) for a in (q, k, v))
+    gq = rng.uniform(0.8, 1.2, D).astype(np.float32)
+    gk = rng.uniform(0.8, 1.2, D).astype(np.float32)
+    axes = (16, 56, 56) if D == 128 else (16, 24, 24)
+    tables = []
+    for i, n in enumerate(lens):   # each sequence has its own position ids
+        pos = np.stack([np.full(n, i), np.arange(n) // 32, np.arange(n) % 32], 1).astype(np.int32)
+        tables.append(L.rope_tables(pos, axes, 10000.0))
+    cos = np.concatenate([c for c, _ in tables]); sin = np.concatenate([s for _, s in tables])
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=D ** -0.5, norm_q=True, norm_k=True,
+                       rope=True, eps=1e-6)
+    ctx.reserve(3 * T * H * D * 2)
+    o = torch.empty((1, T, H * D), device="cuda")
+    L.attention_varlen(ctx, dev(q).half(), dev(k).half(), dev(v).half(), o, cfg, lens,
+                       q_gain=dev(gq), k_gain=dev(gk), cos=dev(cos), sin=dev(sin))
+    ctx.sync()
+    got = host(o)[0]
+    off = 0
+    for i, n in enumerate(lens):
+        sl = slice(off, off + n)
+        rows = (0, n) if n <= 1024 else (n - 300, n)     # long sequence: its last rows
+        want = O.attention_block(q[sl].reshape(n, -1), k[sl].reshape(n, -1),
+                                 v[sl].reshape(n, -1), H, D, D ** -0.5, eps=1e-6,
+                                 q_gain=gq, k_gain=gk, cos=tables[i][0], sin=tables[i][1],
+                                 rows=rows)
+        check(got[sl][rows[0]:rows[1]], want[rows[0]:rows[1]], what=f"seq {i} len {n}")
+        off += n
+
+
+def test_varlen_rejects(ctx):
+    import llmr_attn as L
+    torch = _t()
+    x = torch.zeros((1, 64, 2, 128), device="cuda", dtype=torch.float16)
+    o = torch.empty((1, 64, 256), device="cuda")
+    cfg = L.AttnConfig(n_heads=2, head_dim=128, scale=0.1)
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_varlen(ctx, x, x, x, o, cfg, (30, 30))      # lengths do not sum
+    assert ei.value.status == L.EINVAL
+    with pytest.raises(L.LlmrError) as ei:
+        L.attention_varlen(ctx, x, x, x, o, L.AttnConfig(n_heads=2, head_dim=128, scale=0.1,
+                                                         split_row=8), (32, 32))
+    assert ei.value.status == L.EINVAL
