@@ -147,12 +147,21 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def host_cores() -> int:
+    """Host cores this process may run on."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(case, prep, budget_s=12.0, rows_per_chunk=512, threads=0):
     """The oracle (reference algorithm restated) on host cores (`threads`, 0 =
     all) over a bounded row sample of one batch element. Returns (TFLOP/s,
     rows, seconds)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    O.set_threads(threads if threads > 0 else host_cores())
     S, H, D = case.seq_len, case.n_heads, case.head_dim
 
     def run(rows):
@@ -384,7 +393,7 @@ def cpu_table(args):
     over a row sample of about 8 s, extrapolated to the whole op."""
     import llmr_attn as L
     from llmr_attn import configs as C
-    cores = os.cpu_count() or 1
+    cores = host_cores()
     for name, case in C.CASES.items():
         prep = C.prepare(case, L.rope_tables)
         for threads in (0, 1):
@@ -406,6 +415,8 @@ def run_reference(args):
     from llmr_attn import configs as C
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    cores = host_cores()
+    O.set_threads(cores)     # torchrun sets OMP_NUM_THREADS=1 per process
     case = C.CASES[args.config]
     prep = C.prepare(case, L.rope_tables)
     S, H, D = case.seq_len, case.n_heads, case.head_dim
@@ -423,7 +434,6 @@ def run_reference(args):
         r0 = (r0 + rows) % S
     ms = 1e3 * sum(times) / len(times)
     tflops = 4.0 * H * rows * S * D / (ms / 1e3) / 1e12
-    cores = os.cpu_count()
     sample = (f"per step: {rows} query rows x {H} heads of one batch element, full "
               f"S={S} keys (norm+transpose+RoPE over all tokens, then flash_attention_v2)")
     line = {"metric": METRIC, "value": tflops, "unit": "TFLOP/s", "impl": "reference",
@@ -765,7 +775,7 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, rows, dt = cpu_sample(case, prep)
         line["cpu_baseline"] = {
-            "value": tf, "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "value": tf, "unit": "TFLOP/s", "cores": host_cores(), "kind": "port",
             "sample": f"{rows} of {case.seq_len} query rows x {case.n_heads} heads, "
                       f"{dt:.1f} s, oracle restatement of the reference shaders"}
     if rank == 0:

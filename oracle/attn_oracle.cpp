@@ -57,6 +57,17 @@ extern "C" float orc_round_bf16(float x) {
   return u2f(u);
 }
 
+// Thread count for every parallel loop of this library (0 keeps the OpenMP
+// default). Launchers such as torchrun set OMP_NUM_THREADS=1 per process;
+// the CPU baseline sets the host's core count explicitly instead.
+extern "C" void orc_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 static int pick_threads(int n) {
 #ifdef _OPENMP
   return n > 0 ? n : omp_get_max_threads();

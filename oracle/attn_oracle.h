@@ -24,6 +24,7 @@ extern "C" {
 
 /* Round an fp32 value to IEEE binary16 (round-to-nearest-even), widen back. */
 float orc_round_f16(float x);
+void orc_set_threads(int n);
 /* Round an fp32 value to bfloat16 (round-to-nearest-even), widen back. */
 float orc_round_bf16(float x);
 

@@ -29,6 +29,7 @@ def _load():
                               ctypes.c_int, ctypes.c_double)
     sig = {
         "orc_round_f16": (f32, [f32]),
+        "orc_set_threads": (None, [ctypes.c_int]),
         "orc_round_bf16": (f32, [f32]),
         "orc_batch_head_norm": (None, [vp, vp, u32, u32, u32, f32]),
         "orc_transpose_heads": (None, [vp, vp, u32, u32, u32, u32]),
@@ -57,6 +58,11 @@ def _c(a, dtype=np.float32):
 
 def _p(a):
     return None if a is None else a.ctypes.data
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads for all later oracle calls (0 keeps the default)."""
+    lib.orc_set_threads(int(n))
 
 
 def round_f16(x: float) -> float:
