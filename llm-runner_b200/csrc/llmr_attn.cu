@@ -14,6 +14,7 @@
 #include <math.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <string>
@@ -167,6 +168,28 @@ int launch_out_proj(llmr_ctx *ctx, const CUtensorMap &mx, const CUtensorMap &mw0
   const int grid = p.tiles < sms ? p.tiles : sms;
   out_proj_kernel<BF16><<<grid, C::THREADS, kProjSmemBytes, ctx->stream>>>(mx, mw0, mw1, p);
   return after_launch(ctx, "out_proj");
+}
+
+template <int D, bool BF16>
+int launch_qkv_pair(llmr_ctx *ctx, const void *x, long long x_rs, const void *w, QkvParams &p,
+                    long long hidden) {
+  using C = Qkv2Cfg<D>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    CUDA_TRY(ctx, cudaFuncSetAttribute(qkv_proj_pair_kernel<D, BF16>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set = true;
+  }
+  CUtensorMap mx, mw;
+  int rc;
+  if ((rc = make_map2d(ctx, &mx, x, hidden, p.M, x_rs, C::BM))) return rc;
+  if ((rc = make_map2d(ctx, &mw, w, hidden, 3LL * p.H * D, hidden, C::BN / 2))) return rc;
+  const int pair_tiles = (p.M + 2 * C::BM - 1) / (2 * C::BM) * p.n_tiles;
+  const int pairs_max = (ctx->num_sms > 0 ? ctx->num_sms : 148) / 2;
+  const int grid = 2 * (pair_tiles < pairs_max ? pair_tiles : pairs_max);
+  qkv_proj_pair_kernel<D, BF16><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mx, mw, p);
+  return after_launch(ctx, "qkv_proj_pair");
 }
 
 template <int D, typename OutT>
@@ -550,6 +573,15 @@ int llmr_qkv_project(llmr_ctx *ctx, const llmr_qkv_desc *d, const void *x, const
   const int BN = wide ? 256 : 128;
   p.n_tiles = (int)(3 * H * D / BN);
   p.tiles = (int)((p.M + 127) / 128) * p.n_tiles;
+  // 256-column tiles run on CTA pairs (tcgen05 cta_group::2) unless
+  // LLMR_QKV_SINGLE_CTA is set (for comparisons).
+  static const bool single = getenv("LLMR_QKV_SINGLE_CTA") != nullptr;
+  if (wide && !single) {
+    if (D == 128) return bf ? launch_qkv_pair<128, true>(ctx, x, x_rs, w, p, K)
+                            : launch_qkv_pair<128, false>(ctx, x, x_rs, w, p, K);
+    return bf ? launch_qkv_pair<64, true>(ctx, x, x_rs, w, p, K)
+              : launch_qkv_pair<64, false>(ctx, x, x_rs, w, p, K);
+  }
   if (D == 128) {
     if (wide) return bf ? launch_qkv<128, 256, true>(ctx, x, x_rs, w, p, K)
                         : launch_qkv<128, 256, false>(ctx, x, x_rs, w, p, K);
