@@ -64,6 +64,10 @@ def parse():
                     help="the CFG pair with different text lengths (Z-Image shapes: 256 + 4096 "
                          "and 0 + 4096 tokens, H30 D128 bf16, norm + RoPE) as one packed "
                          "llmr_attention_varlen call against two llmr_attention_fused calls")
+    ap.add_argument("--vae", action="store_true",
+                    help="the VAE mid-block attention (vae_attention: one head, fp32 [S, C], "
+                         "128x128 latent = 16384 tokens, D = 512 and 384) on the wide-head "
+                         "kernel, end to end through the mirror, and the oracle on the host")
     ap.add_argument("--cpu-table", action="store_true",
                     help="only the CPU baseline: the oracle on all host cores and on 1 core, "
                          "every configuration, a bounded row sample each")
@@ -388,6 +392,96 @@ def varlen_bench(args):
     ctx.close()
 
 
+def vae_bench(args):
+    """vae_attention at a 1024x1024 image's latent (128 x 128 = 16384 tokens),
+    one head of 512 (Flux / Z-Image VAE) and of 384 (Qwen VAE), fp32 [S, C]
+    in and out as the reference binds them. Device-resident inputs with the
+    L2 flushed per step (kernel and cast times from the op's own events), the
+    whole mirror call from pinned host buffers (e2e), and the oracle
+    restatement of the shader on all host cores over a row sample."""
+    import numpy as np
+    import torch
+
+    import llmr_attn as L
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    peak, _, kind = peaks()
+    cores = host_cores()
+    O.set_threads(cores)
+    S = 16384
+    ctx = L.Context(0)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for D in (512, 384):
+        g = torch.Generator(device="cuda").manual_seed(D)
+        q, k, v = (torch.randn((S, D), device="cuda", generator=g) for _ in range(3))
+        o = torch.empty((S, D), device="cuda")
+        ctx.reserve(3 * S * D * 2)
+        scale = D ** -0.5
+
+        def call():
+            L.vae_attention(ctx, q, k, v, o, D, 1, S, scale)
+
+        for _ in range(max(args.warmup, 3)):
+            call()
+        torch.cuda.synchronize()
+        ctx.profile(True)
+        tot, cast, attn = [], [], []
+        l0 = ctx.launches
+        for _ in range(args.steps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            call()
+            b.record()
+            c_ms, k_ms = ctx.profile_read()
+            torch.cuda.synchronize()
+            tot.append(a.elapsed_time(b))
+            cast.append(c_ms)
+            attn.append(k_ms)
+        launches = (ctx.launches - l0) / args.steps
+        ctx.profile(False)
+        # End to end: pinned host Q, K, V -> device, the call, O -> pinned host.
+        hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+        ho = torch.empty((S, D)).pin_memory()
+        e2e = []
+        for _ in range(min(args.steps, 10)):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            q.copy_(hq, non_blocking=True)
+            k.copy_(hk, non_blocking=True)
+            v.copy_(hv, non_blocking=True)
+            call()
+            ho.copy_(o, non_blocking=True)
+            b.record()
+            torch.cuda.synchronize()
+            e2e.append(a.elapsed_time(b))
+        flops = 4.0 * S * S * D
+        ms, cast_ms, attn_ms = (sum(x) / len(x) for x in (tot, cast, attn))
+        e2e_ms = sum(e2e) / len(e2e)
+        # The oracle (the shader's fp32 restatement) over a row sample.
+        nq, nk, nv = (x.numpy() for x in (hq, hk, hv))
+        rows = 32
+        t0 = time.perf_counter()
+        O.vae_attention(nq, nk, nv, D, 1, S, scale, rows=(0, rows))
+        cpu_s = time.perf_counter() - t0
+        cpu_tf = flops * rows / S / cpu_s / 1e12
+        print(json.dumps({
+            "vae": f"vae_attention S{S} D{D} fp32 [S,C]", "steps": args.steps,
+            "ms_per_call": ms, "cast_ms": cast_ms, "kernel_ms": attn_ms,
+            "tflops_call": flops / ms / 1e9, "tflops_kernel": flops / attn_ms / 1e9,
+            "kernel_mma_tflops": 1.5 * flops / attn_ms / 1e9,
+            "kernel_frac_of_peak": flops / attn_ms / 1e9 / peak, "peak_tflops": peak,
+            "peak_source": kind, "gpu_launches_per_call": launches,
+            "e2e": {"ms": e2e_ms, "tflops": flops / e2e_ms / 1e9,
+                    "h2d_bytes": 3 * S * D * 4, "d2h_bytes": S * D * 4},
+            "cpu_baseline": {"tflops": cpu_tf, "cores": cores, "kind": "port",
+                             "sample": f"{rows} of {S} query rows",
+                             "full_op_ms_extrapolated": flops / (cpu_tf * 1e12) * 1e3}}),
+            flush=True)
+    ctx.close()
+
+
 def cpu_table(args):
     """The oracle per configuration on all host cores and on one core, each
     over a row sample of about 8 s, extrapolated to the whole op."""
@@ -595,6 +689,9 @@ def main():
         return
     if args.varlen:
         varlen_bench(args)
+        return
+    if args.vae:
+        vae_bench(args)
         return
     if args.profile_run:
         profile_run(args)

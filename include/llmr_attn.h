@@ -191,6 +191,20 @@ int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k,
                            uint32_t head_dim, uint32_t n_heads,
                            uint32_t seq_len, float scale);
 
+/* vae_attention (lib/shaders/diffusion.slang:1828-1975; VaeAttentionParams
+ * {head_dim, n_heads, seq_len, scale, channels}, dispatched by
+ * dependencies/zimage.c3l/flux_vae.c3:526-538 with one head of 512 and
+ * dependencies/qwen_edit.c3l/qwen_vae.c3:459-464 with one head of 384).
+ * q,k,v,o: [seq_len, channels] fp32, head h at columns [h*head_dim,
+ * (h+1)*head_dim). head_dim 64, 128, 384 or 512. Computed on the tensor
+ * cores with fp16 operands and fp32 accumulation (workspace
+ * 3*seq_len*n_heads*head_dim*2 bytes); LLMR_EXACT through
+ * llmr_attention_fused gives the fp32 path. */
+int llmr_vae_attention(llmr_ctx *ctx, const float *q, const float *k,
+                       const float *v, float *o, uint32_t head_dim,
+                       uint32_t n_heads, uint32_t seq_len, float scale,
+                       uint32_t channels);
+
 /* split_qkv (dependencies/depth_anything.c3l/shaders/depth.slang:40-58;
  * {dim, n_rows}): qkv[n_rows, 3*dim] -> q,k,v [n_rows, dim]. */
 int llmr_split_qkv(llmr_ctx *ctx, const float *qkv, float *q, float *k,
@@ -208,7 +222,9 @@ int llmr_split_qkv(llmr_ctx *ctx, const float *qkv, float *q, float *k,
  * pointers at column offsets 0, H*D, 2*H*D with row stride 3*H*D (replaces
  * split_qkv). O is always [B][S][H*D] (row stride o_row_stride). */
 typedef struct {
-  uint32_t batch, n_heads, seq_len, head_dim; /* head_dim 64 or 128 */
+  /* head_dim 64 or 128; 384 or 512 (the VAE attention) without
+   * LLMR_NORM_Q/NORM_K/ROPE/MERGE and not in llmr_attention_varlen */
+  uint32_t batch, n_heads, seq_len, head_dim;
   llmr_dtype in_dtype;                        /* dtype of q, k, v */
   llmr_dtype out_dtype;                       /* dtype of o */
   llmr_layout layout;                         /* layout of q, k, v */

@@ -103,17 +103,14 @@ struct ExactParams {
   float *lse;  // optional [B][H][S]
 };
 
-template <int D>
-__global__ void __launch_bounds__(128)
-    attn_exact_f32_kernel(const float *Q, const float *K, const float *V,
-                          ExactParams p) {
-  // Static shared memory stays under 48 KB: D=128 uses 32-key tiles and 4
-  // rows per warp, D=64 64-key tiles and 8 rows per warp.
-  constexpr int KT = D == 128 ? 32 : 64, NC = KT / 32;
-  constexpr int RPW = D == 128 ? 4 : 8, DL = D / 32;
-  __shared__ float sK[KT][D + 1];
-  __shared__ float sV[KT][D];
-  __shared__ float sQ[4 * RPW][D];
+// Body of the exact kernels: KT keys per shared-memory tile, RPW query rows
+// per warp, sK [KT][D+1] (padded: lane = key reads are conflict-free),
+// sV [KT][D], sQ [4*RPW][D].
+template <int D, int KT, int RPW>
+__device__ __forceinline__ void attn_exact_body(const float *Q, const float *K, const float *V,
+                                                const ExactParams &p, float (*sK)[D + 1],
+                                                float (*sV)[D], float (*sQ)[D]) {
+  constexpr int NC = KT / 32, DL = D / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bh = blockIdx.y, b = bh / p.H, h = bh % p.H;
   const long long head_off = (long long)bh * p.S * D;
@@ -188,6 +185,37 @@ __global__ void __launch_bounds__(128)
     for (int e = 0; e < DL; e++) dst[lane + 32 * e] = acc[r][e] / l[r];
     if (p.lse != nullptr && lane == 0) p.lse[(long long)bh * p.S + qr] = m[r] + logf(l[r]);
   }
+}
+
+template <int D>
+__global__ void __launch_bounds__(128)
+    attn_exact_f32_kernel(const float *Q, const float *K, const float *V,
+                          ExactParams p) {
+  // Static shared memory stays under 48 KB: D=128 uses 32-key tiles and 4
+  // rows per warp, D=64 64-key tiles and 8 rows per warp.
+  constexpr int KT = D == 128 ? 32 : 64;
+  constexpr int RPW = D == 128 ? 4 : 8;
+  __shared__ float sK[KT][D + 1];
+  __shared__ float sV[KT][D];
+  __shared__ float sQ[4 * RPW][D];
+  attn_exact_body<D, KT, RPW>(Q, K, V, p, sK, sV, sQ);
+}
+
+// Wide heads (D = 384 or 512, the VAE attention): 32-key tiles and 4 rows
+// per warp in dynamic shared memory (exact_wide_smem bytes).
+constexpr int kExactWideRows = 4;
+__host__ __device__ constexpr int exact_wide_smem(int D) {
+  return (32 * (D + 1) + 32 * D + 4 * kExactWideRows * D) * (int)sizeof(float);
+}
+
+template <int D>
+__global__ void __launch_bounds__(128)
+    attn_exact_wide_kernel(const float *Q, const float *K, const float *V, ExactParams p) {
+  extern __shared__ float xsm[];
+  float(*sK)[D + 1] = reinterpret_cast<float(*)[D + 1]>(xsm);
+  float(*sV)[D] = reinterpret_cast<float(*)[D]>(xsm + 32 * (D + 1));
+  float(*sQ)[D] = reinterpret_cast<float(*)[D]>(xsm + 32 * (D + 1) + 32 * D);
+  attn_exact_body<D, 32, kExactWideRows>(Q, K, V, p, sK, sV, sQ);
 }
 
 // Combine two normalised partial results over disjoint key sets:

@@ -21,6 +21,7 @@
 
 #include "../../include/llmr_attn.h"
 #include "fa_tc.cuh"
+#include "fa_wide.cuh"
 #include "kernels_misc.cuh"
 #include "qkv_proj.cuh"
 
@@ -338,6 +339,115 @@ void default_strides(const llmr_attn_desc *d, uint64_t rs_in, uint64_t bs_in, ui
   out[1] = rs_in ? (long long)rs_in : rs;
   out[2] = hs_in ? (long long)hs_in : hs;
 }
+
+// ---------------------------------------------------------------- wide heads
+
+// The largest dynamic shared memory a block of this device may opt into.
+int smem_optin(llmr_ctx *ctx) {
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, ctx->device) !=
+      cudaSuccess)
+    return 0;
+  return v;
+}
+
+template <int D, typename OutT>
+int launch_fa_wide(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
+                   const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
+                   long long o_rs, long long o_bs, float *lse) {
+  using C = FaWideCfg<D>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (smem_optin(ctx) < C::SMEM_BYTES)
+      return fail(ctx, LLMR_ECUDA, "fa_wide_tc needs %d bytes of shared memory per block",
+                  C::SMEM_BYTES);
+    CUDA_TRY(ctx, cudaFuncSetAttribute(fa_wide_tc_kernel<D, OutT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set = true;
+  }
+  FaParams p;
+  memset(&p, 0, sizeof p);
+  p.S = S;
+  p.S_kv = S_kv;
+  p.H = H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = o;
+  p.o_row_stride = o_rs;
+  p.o_batch_stride = o_bs;
+  p.lse = lse;
+  p.err = ctx->d_err;
+  const dim3 grid = fa_wide_grid<D>(p, B, ctx->num_sms);
+  fa_wide_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
+  return after_launch(ctx, "fa_wide_tc");
+}
+
+int launch_fa_wide_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
+                       const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S,
+                       int S_kv, float scale, void *o, long long o_rs, long long o_bs,
+                       float *lse) {
+#define LLMR_WIDE_ARGS ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse
+  if (D == 512) {
+    if (od == LLMR_F32) return launch_fa_wide<512, float>(LLMR_WIDE_ARGS);
+    if (od == LLMR_F16) return launch_fa_wide<512, __half>(LLMR_WIDE_ARGS);
+    return launch_fa_wide<512, __nv_bfloat16>(LLMR_WIDE_ARGS);
+  }
+  if (od == LLMR_F32) return launch_fa_wide<384, float>(LLMR_WIDE_ARGS);
+  if (od == LLMR_F16) return launch_fa_wide<384, __half>(LLMR_WIDE_ARGS);
+  return launch_fa_wide<384, __nv_bfloat16>(LLMR_WIDE_ARGS);
+#undef LLMR_WIDE_ARGS
+}
+
+template <typename InT, typename OutT>
+int launch_wide_cast_t(llmr_ctx *ctx, const void *q, const void *k, const void *v,
+                       const long long *qs, const long long *ks, const long long *vs, OutT *out,
+                       int B, int H, int S, int D) {
+  View<InT> vq{static_cast<const InT *>(q), qs[0], qs[1], qs[2]};
+  View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
+  View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
+  constexpr int VIN = 16 / sizeof(InT);
+  auto ok = [&](const void *ptr, const long long *st) {
+    return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && st[0] % VIN == 0 &&
+           st[1] % VIN == 0 && st[2] % VIN == 0;
+  };
+  const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs);
+  const long long groups = (long long)B * H * S * (D / 8);
+  const dim3 grid(grid_for(ctx, groups, 256), 3);
+  if (vec)
+    wide_cast_kernel<InT, OutT, true><<<grid, 256, 0, ctx->stream>>>(vq, vk, vv, out, B, H, S, D);
+  else
+    wide_cast_kernel<InT, OutT, false><<<grid, 256, 0, ctx->stream>>>(vq, vk, vv, out, B, H, S, D);
+  return after_launch(ctx, "wide_cast");
+}
+
+template <typename OutT>
+int launch_wide_cast(llmr_ctx *ctx, llmr_dtype in, const void *q, const void *k, const void *v,
+                     const long long *qs, const long long *ks, const long long *vs, OutT *out,
+                     int B, int H, int S, int D) {
+  if (in == LLMR_F32) return launch_wide_cast_t<float, OutT>(ctx, q, k, v, qs, ks, vs, out, B, H, S, D);
+  if (in == LLMR_F16) return launch_wide_cast_t<__half, OutT>(ctx, q, k, v, qs, ks, vs, out, B, H, S, D);
+  return launch_wide_cast_t<__nv_bfloat16, OutT>(ctx, q, k, v, qs, ks, vs, out, B, H, S, D);
+}
+
+template <int D>
+int launch_exact_wide_t(llmr_ctx *ctx, const float *q, const float *k, const float *v,
+                        const ExactParams &ep) {
+  constexpr int smem = exact_wide_smem(D);
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (smem_optin(ctx) < smem)
+      return fail(ctx, LLMR_ECUDA, "attn_exact_wide needs %d bytes of shared memory", smem);
+    CUDA_TRY(ctx, cudaFuncSetAttribute(attn_exact_wide_kernel<D>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    attr_set = true;
+  }
+  constexpr int rows_per_cta = 4 * kExactWideRows;
+  dim3 grid((ep.S + rows_per_cta - 1) / rows_per_cta, ep.B * ep.H);
+  attn_exact_wide_kernel<D><<<grid, 128, smem, ctx->stream>>>(q, k, v, ep);
+  return after_launch(ctx, "attn_exact_wide");
+}
+
+bool is_wide(int D) { return D == 384 || D == 512; }
 
 }  // namespace
 
@@ -697,10 +807,16 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
   if (!d || !q || !k || !v || !o) return fail(ctx, LLMR_EINVAL, "null argument");
   const int B = d->batch, H = d->n_heads, S = d->seq_len, D = d->head_dim;
   if (B < 1 || H < 1 || S < 1) return fail(ctx, LLMR_EINVAL, "batch, n_heads, seq_len must be >= 1");
-  if (D != 64 && D != 128) return fail(ctx, LLMR_EINVAL, "head_dim %d unsupported (64 or 128)", D);
+  const bool wide = is_wide(D);
+  if (D != 64 && D != 128 && !wide)
+    return fail(ctx, LLMR_EINVAL, "head_dim %d unsupported (64, 128, 384 or 512)", D);
   if ((long long)B * H > 65535) return fail(ctx, LLMR_EINVAL, "batch*n_heads exceeds 65535");
   if (d->in_dtype > LLMR_BF16 || d->out_dtype > LLMR_BF16 || d->layout > LLMR_LAYOUT_BHSD)
     return fail(ctx, LLMR_EINVAL, "bad dtype or layout");
+  if (wide && (d->flags & (LLMR_NORM_Q | LLMR_NORM_K | LLMR_ROPE | LLMR_MERGE)))
+    return fail(ctx, LLMR_EINVAL, "head_dim %d takes no norm, RoPE or merge", D);
+  if (wide && nseq > 0)
+    return fail(ctx, LLMR_EINVAL, "head_dim %d takes no variable-length batch", D);
   if ((d->flags & LLMR_NORM_Q) && !q_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_Q needs q_gain");
   if ((d->flags & LLMR_NORM_K) && !k_gain) return fail(ctx, LLMR_EINVAL, "LLMR_NORM_K needs k_gain");
   if ((d->flags & LLMR_ROPE) && (!cos_t || !sin_t)) return fail(ctx, LLMR_EINVAL, "LLMR_ROPE needs cos/sin tables");
@@ -750,7 +866,8 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
   mark(0);
   if (exact) {
     float *w = static_cast<float *>(ctx->ws);
-    rc = launch_prologue<float>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
+    rc = wide ? launch_wide_cast<float>(ctx, d->in_dtype, q, k, v, qs, ks, vs, w, B, H, S, D)
+              : launch_prologue<float>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
     if (rc) return rc;
     mark(1);
     ExactParams ep;
@@ -763,7 +880,12 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     ep.o_row_stride = o_rs;
     ep.o_head_stride = D;
     ep.lse = lse_out;
-    rc = launch_exact(ctx, D, w, w + plane, w + 2 * plane, ep);
+    if (!wide)
+      rc = launch_exact(ctx, D, w, w + plane, w + 2 * plane, ep);
+    else if (D == 512)
+      rc = launch_exact_wide_t<512>(ctx, w, w + plane, w + 2 * plane, ep);
+    else
+      rc = launch_exact_wide_t<384>(ctx, w, w + plane, w + 2 * plane, ep);
     mark(2);
     ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
     return rc;
@@ -777,7 +899,8 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     if ((rc = make_map(ctx, &mv, v, D, S_kv, H, B, vs[1], vs[2], vs[0]))) return rc;
   } else {
     __half *w = static_cast<__half *>(ctx->ws);
-    rc = launch_prologue<__half>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
+    rc = wide ? launch_wide_cast<__half>(ctx, d->in_dtype, q, k, v, qs, ks, vs, w, B, H, S, D)
+              : launch_prologue<__half>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
     if (rc) return rc;
     // Workspace layout: dense [3][B][H][S][D] fp16.
     const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
@@ -786,8 +909,12 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     if ((rc = make_map(ctx, &mv, w + 2 * plane, D, S, H, B, rs, hs, bs))) return rc;
   }
   mark(1);
-  rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
-                        o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0, nseq, seq_off);
+  if (wide)
+    rc = launch_fa_wide_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
+                            o_bs, lse_out);
+  else
+    rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
+                          o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0, nseq, seq_off);
   mark(2);
   ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
   return rc;
@@ -908,6 +1035,25 @@ int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k, const 
   ep.o_head_stride = (long long)seq_len * head_dim;
   ep.lse = nullptr;
   return launch_exact(ctx, (int)head_dim, q, k, v, ep);
+}
+
+int llmr_vae_attention(llmr_ctx *ctx, const float *q, const float *k, const float *v, float *o,
+                       uint32_t head_dim, uint32_t n_heads, uint32_t seq_len, float scale,
+                       uint32_t channels) {
+  if ((uint64_t)channels < (uint64_t)n_heads * head_dim)
+    return fail(ctx, LLMR_EINVAL, "channels %u < n_heads * head_dim", channels);
+  llmr_attn_desc d;
+  memset(&d, 0, sizeof d);
+  d.batch = 1;
+  d.n_heads = n_heads;
+  d.seq_len = seq_len;
+  d.head_dim = head_dim;
+  d.in_dtype = LLMR_F32;
+  d.out_dtype = LLMR_F32;
+  d.layout = LLMR_LAYOUT_BSHD;
+  d.scale = scale;
+  d.q_row_stride = d.k_row_stride = d.v_row_stride = d.o_row_stride = channels;
+  return llmr_attention_fused(ctx, &d, q, k, v, nullptr, nullptr, nullptr, nullptr, o, nullptr);
 }
 
 int llmr_batch_head_norm(llmr_ctx *ctx, float *data, const float *gain, uint32_t n_heads,

@@ -169,4 +169,54 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Prologue of the wide-head path (D = 384 / 512, the VAE attention, which has
+// no norm or RoPE): Q, K, V from strided views of any input type to dense
+// [3][B][H][S][D] OutT (fp16 RNE for the tensor-core kernel, fp32 for the
+// exact one). Grid (x, 3): blockIdx.y selects the tensor; a thread converts
+// 8 consecutive elements of one row. VEC: bases and strides allow 16-byte
+// loads (checked on the host).
+template <typename InT, typename OutT, bool VEC>
+__global__ void __launch_bounds__(256)
+    wide_cast_kernel(View<InT> q, View<InT> k, View<InT> v, OutT *out, int B, int H, int S,
+                     int D) {
+  const int t = blockIdx.y;
+  const InT *base = t == 0 ? q.base : (t == 1 ? k.base : v.base);
+  const long long bs = t == 0 ? q.bs : (t == 1 ? k.bs : v.bs);
+  const long long rs = t == 0 ? q.rs : (t == 1 ? k.rs : v.rs);
+  const long long hs = t == 0 ? q.hs : (t == 1 ? k.hs : v.hs);
+  const int gpr = D / 8;  // 8-element groups per row
+  const long long groups = (long long)B * H * S * gpr;
+  OutT *dst0 = out + (long long)t * B * H * S * D;
+  constexpr int VIN = 16 / sizeof(InT), VOUT = 16 / sizeof(OutT);
+  for (long long g = (long long)blockIdx.x * blockDim.x + threadIdx.x; g < groups;
+       g += (long long)gridDim.x * blockDim.x) {
+    const int d = (int)(g % gpr) * 8;
+    const long long row = g / gpr;  // (b * H + h) * S + s
+    const int s = (int)(row % S);
+    const long long bh = row / S;
+    const int h = (int)(bh % H), b = (int)(bh / H);
+    const InT *src = base + (long long)b * bs + (long long)s * rs + (long long)h * hs + d;
+    float x[8];
+    if (VEC) {
+#pragma unroll
+      for (int c = 0; c < 8 / VIN; c++) {
+        const Pack<InT, VIN> pk = *reinterpret_cast<const Pack<InT, VIN> *>(src + c * VIN);
+#pragma unroll
+        for (int e = 0; e < VIN; e++) x[c * VIN + e] = to_f32<InT>(pk.v[e]);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) x[e] = to_f32<InT>(src[e]);
+    }
+    OutT *dst = dst0 + row * D + d;
+#pragma unroll
+    for (int c = 0; c < 8 / VOUT; c++) {
+      Pack<OutT, VOUT> po;
+#pragma unroll
+      for (int e = 0; e < VOUT; e++) po.v[e] = from_f32<OutT>(x[c * VOUT + e]);
+      *reinterpret_cast<Pack<OutT, VOUT> *>(dst + c * VOUT) = po;
+    }
+  }
+}
+
 }  // namespace llmr

@@ -12,6 +12,7 @@ argument order, over the C-ABI library `libllmr_attn.so` (include/llmr_attn.h):
     transpose_heads(ctx, inp, out, seq_len, n_heads, head_dim, direction)
     mrope(ctx, data, cos, sin, seq_len, n_heads)
     spatial_attention(ctx, q, k, v, scores, o, head_dim, n_heads, seq_len, scale)
+    vae_attention(ctx, q, k, v, o, head_dim, n_heads, seq_len, scale, channels)
     split_qkv(ctx, qkv, q, k, v, dim, n_rows)
 
 plus the fused op `attention_fused` that replaces the whole 8-dispatch
@@ -127,6 +128,7 @@ def _load() -> ctypes.CDLL:
         "llmr_mrope": (i32, [vp, vp, vp, vp, u32, u32]),
         "llmr_spatial_attention": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, f32]),
         "llmr_split_qkv": (i32, [vp, vp, vp, vp, vp, u32, u32]),
+        "llmr_vae_attention": (i32, [vp, vp, vp, vp, vp, u32, u32, u32, f32, u32]),
         "llmr_attention_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(AttnDesc)]),
         "llmr_attention_fused": (i32, [vp, ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                        vp, vp, vp, vp]),
@@ -274,6 +276,17 @@ def spatial_attention(ctx: Context, q, k, v, scores, o, head_dim: int, n_heads: 
     ctx.check(lib.llmr_spatial_attention(ctx.handle, _ptr(q), _ptr(k), _ptr(v),
                                          _ptr(scores), _ptr(o), head_dim, n_heads,
                                          seq_len, scale))
+
+
+def vae_attention(ctx: Context, q, k, v, o, head_dim: int, n_heads: int, seq_len: int,
+                  scale: float, channels: int = 0) -> None:
+    """diffusion.slang:1828-1975. q,k,v,o fp32 [S, C] (C = channels, default
+    n_heads*head_dim), head h at columns [h*D, (h+1)*D); head_dim 64, 128,
+    384 or 512. Tensor cores with fp16 operands; needs a workspace of
+    3*S*H*D*2 bytes (ctx.reserve)."""
+    channels = channels or n_heads * head_dim
+    ctx.check(lib.llmr_vae_attention(ctx.handle, _ptr(q), _ptr(k), _ptr(v), _ptr(o),
+                                     head_dim, n_heads, seq_len, scale, channels))
 
 
 def split_qkv(ctx: Context, qkv, q, k, v, dim: int, n_rows: int) -> None:
@@ -567,7 +580,8 @@ def rope_tables(pos: np.ndarray, axes_dims: Sequence[int], theta: float):
 __all__ = [
     "Context", "LlmrError", "AttnConfig", "AttnDesc", "make_desc", "workspace_bytes",
     "flash_attention_v2", "batch_head_norm", "perhead_rmsnorm", "transpose_heads",
-    "mrope", "spatial_attention", "split_qkv", "attention_fused", "attention_merge",
-    "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async", "copy2d_async", "qkv_project", "QkvDesc", "out_project", "ProjDesc", "attention_varlen", "IpcHandle", "LIB_PATH",
-    "lib",
+    "mrope", "spatial_attention", "vae_attention", "split_qkv", "attention_fused",
+    "attention_merge", "rope_tables", "DeviceBuffer", "PeerMapping", "copy_async",
+    "copy2d_async", "qkv_project", "QkvDesc", "out_project", "ProjDesc", "attention_varlen",
+    "IpcHandle", "LIB_PATH", "lib",
 ]

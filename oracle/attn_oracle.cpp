@@ -339,6 +339,85 @@ extern "C" void orc_spatial_attention(const float *q, const float *k,
   }
 }
 
+// vae_attention: lib/shaders/diffusion.slang:1846-1975. One (head, query) per
+// 256-lane workgroup over Q, K, V, O in [S, C] (head h at columns
+// [h*D, h*D+D)); keys in tiles of 4096 (:1878-1881) with a running max and
+// sum (:1921-1960). Per tile: scores = (q . k) * scale with d ascending
+// (:1884-1889); the tile max and sum are 256 lane partials (lane gi takes
+// keys gi, gi+256, ...) folded by the shader's tree (:1893-1922); the output
+// is rescaled by alpha = exp(old_max - new_max) and gains sum_i p_i v_i with
+// i ascending (:1940-1951); the end multiplies by 1/run_sum (:1964-1972).
+static void vae_row(const float *Q, const float *K, const float *V, float *O,
+                    uint32_t D, uint32_t S, uint32_t C, float scale,
+                    uint32_t head, uint32_t qpos, float *sc, float *acc) {
+  const uint32_t TILE = 4096;
+  const uint64_t hd = (uint64_t)head * D;
+  const float *qr = Q + (uint64_t)qpos * C + hd;
+  for (uint32_t d = 0; d < D; d++) acc[d] = 0.0f;
+  float run_max = -1.0e30f, run_sum = 0.0f;
+  float sh[256];
+  for (uint32_t t0 = 0; t0 < S; t0 += TILE) {
+    const uint32_t len = (S - t0 < TILE) ? S - t0 : TILE;
+    for (uint32_t i = 0; i < len; i++) {
+      const float *kr = K + (uint64_t)(t0 + i) * C + hd;
+      float dot = 0.0f;
+      for (uint32_t d = 0; d < D; d++) dot += qr[d] * kr[d];
+      sc[i] = dot * scale;
+    }
+    for (uint32_t gi = 0; gi < 256; gi++) {
+      float mx = -1.0e30f;
+      for (uint32_t i = gi; i < len; i += 256) mx = fmaxf(mx, sc[i]);
+      sh[gi] = mx;
+    }
+    for (uint32_t s = 128; s > 0; s >>= 1)
+      for (uint32_t gi = 0; gi < s; gi++) sh[gi] = fmaxf(sh[gi], sh[gi + s]);
+    const float tile_max = sh[0];
+    const float new_max = fmaxf(run_max, tile_max);
+    const float alpha = expf(run_max - new_max);
+    for (uint32_t gi = 0; gi < 256; gi++) {
+      float sum = 0.0f;
+      for (uint32_t i = gi; i < len; i += 256) {
+        const float e = expf(sc[i] - new_max);
+        sc[i] = e;
+        sum += e;
+      }
+      sh[gi] = sum;
+    }
+    for (uint32_t s = 128; s > 0; s >>= 1)
+      for (uint32_t gi = 0; gi < s; gi++) sh[gi] += sh[gi + s];
+    const float tile_sum = sh[0];
+    for (uint32_t d = 0; d < D; d++) {
+      acc[d] *= alpha;
+      float va = 0.0f;
+      for (uint32_t i = 0; i < len; i++) va += sc[i] * V[(uint64_t)(t0 + i) * C + hd + d];
+      acc[d] += va;
+    }
+    run_max = new_max;
+    run_sum = run_sum * alpha + tile_sum;
+  }
+  const float inv = 1.0f / run_sum;
+  float *orow = O + (uint64_t)qpos * C + hd;
+  for (uint32_t d = 0; d < D; d++) orow[d] = acc[d] * inv;
+}
+
+extern "C" void orc_vae_attention(const float *q, const float *k, const float *v,
+                                  float *o, uint32_t D, uint32_t H, uint32_t S,
+                                  float scale, uint32_t C, uint32_t row_begin,
+                                  uint32_t row_end, int n_threads) {
+  if (row_end > S) row_end = S;
+  if (row_begin >= row_end) return;
+  const int64_t nr = row_end - row_begin, total = nr * H;
+  const int nt = pick_threads(n_threads);
+#pragma omp parallel num_threads(nt)
+  {
+    std::vector<float> sc(S < 4096 ? S : 4096), acc(D);
+#pragma omp for schedule(dynamic, 4)
+    for (int64_t t = 0; t < total; t++)
+      vae_row(q, k, v, o, D, S, C, scale, (uint32_t)(t / nr), row_begin + (uint32_t)(t % nr),
+              sc.data(), acc.data());
+  }
+}
+
 // split_qkv: dependencies/depth_anything.c3l/shaders/depth.slang:40-58.
 extern "C" void orc_split_qkv(const float *qkv, float *q, float *k, float *v,
                               uint32_t dim, uint32_t n_rows) {

@@ -63,6 +63,15 @@ void orc_spatial_attention(const float *q, const float *k, const float *v,
                            uint32_t seq_len, float scale, uint32_t row_begin,
                            uint32_t row_end, int n_threads);
 
+/* vae_attention: single- or multi-head attention on Q, K, V, O in [S, C]
+ * (head h at columns [h*D, h*D+D)), exact fp32 softmax over 4096-key tiles.
+ * lib/shaders/diffusion.slang:1846-1975 (VaeAttentionParams {head_dim,
+ * n_heads, seq_len, scale, channels}). Rows [row_begin,row_end) only. */
+void orc_vae_attention(const float *q, const float *k, const float *v,
+                       float *o, uint32_t head_dim, uint32_t n_heads,
+                       uint32_t seq_len, float scale, uint32_t channels,
+                       uint32_t row_begin, uint32_t row_end, int n_threads);
+
 /* split_qkv: [N, 3*dim] -> three [N, dim].
  * dependencies/depth_anything.c3l/shaders/depth.slang:40-58. */
 void orc_split_qkv(const float *qkv, float *q, float *k, float *v,

@@ -36,6 +36,7 @@ def _load():
         "orc_mrope": (None, [vp, vp, vp, u32, u32, u32]),
         "orc_flash_attention_v2": (None, [vp, vp, vp, vp, u32, u32, u32, f32, u32, u32, i32]),
         "orc_spatial_attention": (None, [vp, vp, vp, vp, u32, u32, u32, f32, u32, u32, i32]),
+        "orc_vae_attention": (None, [vp, vp, vp, vp, u32, u32, u32, f32, u32, u32, u32, i32]),
         "orc_split_qkv": (None, [vp, vp, vp, vp, u32, u32]),
         "orc_rope_tables": (None, [vp, u32, u32, vp, f32, vp, vp]),
         "orc_attention_block": (None, [vp, vp, vp, vp, u32, u32, u32, f32, f32, vp, vp, vp,
@@ -112,6 +113,19 @@ def spatial_attention(q, k, v, head_dim, n_heads, seq_len, scale, rows=None, thr
     r0, r1 = rows or (0, seq_len)
     lib.orc_spatial_attention(q.ctypes.data, k.ctypes.data, v.ctypes.data, o.ctypes.data,
                               head_dim, n_heads, seq_len, scale, r0, r1, threads)
+    return o
+
+
+def vae_attention(q, k, v, head_dim, n_heads, seq_len, scale, channels=None, rows=None,
+                  threads=0):
+    """q,k,v [S, C] -> O [S, C] (rows outside `rows` are zero); C defaults to
+    n_heads * head_dim."""
+    q, k, v = _c(q), _c(k), _c(v)
+    channels = channels or n_heads * head_dim
+    o = np.zeros((seq_len, channels), np.float32)
+    r0, r1 = rows or (0, seq_len)
+    lib.orc_vae_attention(q.ctypes.data, k.ctypes.data, v.ctypes.data, o.ctypes.data,
+                          head_dim, n_heads, seq_len, scale, channels, r0, r1, threads)
     return o
 
 

@@ -90,6 +90,9 @@ def test_workspace_sizes():
     assert L.workspace_bytes(L.make_desc(raw, 1, 1370, L.F16, L.F16)) == 0
     ex = L.AttnConfig(n_heads=4, head_dim=64, scale=0.125, exact=True)
     assert L.workspace_bytes(L.make_desc(ex, 1, 256, L.F32, L.F32)) == 3 * 4 * 256 * 64 * 4
+    vae = L.AttnConfig(n_heads=1, head_dim=512, scale=512 ** -0.5)
+    assert L.workspace_bytes(L.make_desc(vae, 1, 16384, L.F32, L.F32)) == 3 * 16384 * 512 * 2
+    assert L.workspace_bytes(L.make_desc(vae, 1, 16384, L.F16, L.F16)) == 0
 
 
 def test_configs_flops_and_shapes():
