@@ -403,15 +403,16 @@ def vae_bench(args):
     import torch
 
     import llmr_attn as L
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
     peak, _, kind = peaks()
-    cores = host_cores()
-    O.set_threads(cores)
+    if not args.profile_run:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        cores = host_cores()
+        O.set_threads(cores)
     S = 16384
     ctx = L.Context(0)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
-    for D in (512, 384):
+    for D in ((512,) if args.profile_run else (512, 384)):
         g = torch.Generator(device="cuda").manual_seed(D)
         q, k, v = (torch.randn((S, D), device="cuda", generator=g) for _ in range(3))
         o = torch.empty((S, D), device="cuda")
@@ -420,6 +421,13 @@ def vae_bench(args):
 
         def call():
             L.vae_attention(ctx, q, k, v, o, D, 1, S, scale)
+
+        if args.profile_run:
+            # W + K calls (cast + wide kernel each) and nothing else, for ncu.
+            for _ in range(args.warmup + args.steps):
+                call()
+            torch.cuda.synchronize()
+            break
 
         for _ in range(max(args.warmup, 3)):
             call()
@@ -690,6 +698,7 @@ def main():
     if args.varlen:
         varlen_bench(args)
         return
+
     if args.vae:
         vae_bench(args)
         return

@@ -436,4 +436,430 @@ __global__ void __launch_bounds__(192, 1)
   if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
 }
 
+// ---------------------------------------------------------------------------
+// The same attention on CTA pairs (2-CTA clusters, tcgen05 cta_group::2). The
+// single-CTA kernel above keeps Q resident (128 KB at D = 512), which leaves
+// a 96 KB K/V ring against ~190 KB of K and V per key block: it runs out of
+// loads in flight (tensor pipe ~30 % busy at ~14 % of L2 throughput). Here a
+// pair computes 256 query rows (each CTA holds its own 128 rows of Q) with
+// M = 256 MMAs, so each CTA loads only half of every operand it shares:
+//   S = Q K^T : N = 128 keys, each CTA loads 64 of them (8 KB per K chunk);
+//   O = P V   : N = the output part's columns, each CTA loads half of them.
+// Output parts: columns [256p, min(256p + 256, D)), p = 0, 1 (D = 512:
+// 256 + 256; D = 384: 256 + 128); a unit is (b, h, part, 256-query tile).
+// The even CTA issues every MMA and owns the barriers that count both CTAs'
+// TMA bytes (q_full, k_full, v_full) or both CTAs' softmax warps (p_half,
+// o_empty); every MMA commit is delivered to the matching barrier of both
+// CTAs (no multicast). Roles, TMEM use and the barrier protocol otherwise
+// follow fa_wide_tc_kernel.
+template <int D>
+struct FaWide2Cfg {
+  static_assert(D == 384 || D == 512, "wide attention pair kernel: D = 384 or 512");
+  static constexpr int BM = 128;                 // query rows per CTA
+  static constexpr int BN = 128;                 // keys per block (per pair)
+  static constexpr int ATOM = 128 * 128;         // 64 columns x 128 rows, SW128
+  static constexpr int QCH = D / 64;             // Q / K column chunks
+  static constexpr int Q_BYTES = QCH * ATOM;
+  static constexpr int K_BYTES = 64 * 128;       // 64 keys x 64 columns (this CTA's half)
+  static constexpr int V_SLOT = 2 * ATOM;        // up to 128 of a part's columns
+  static constexpr int NSTK = 8;                 // K ring slots
+  static constexpr int NSTV = D == 512 ? 1 : 2;  // V ring slots
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = Q_BYTES;
+  static constexpr int V_OFF = K_OFF + NSTK * K_BYTES;
+  static constexpr int BAR_OFF = V_OFF + NSTV * V_SLOT;
+  // q_full, q_empty, k_full[NSTK], k_empty[NSTK], v_full[NSTV], v_empty[NSTV],
+  // s_full[2], p_half[2][2], pv_done, o_full, o_empty, drain; tmem word; abort
+  static constexpr int NBAR = 2 + 2 * NSTK + 2 * NSTV + 2 + 4 + 4;
+  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;
+  static_assert(SMEM_BYTES <= 232448, "shared memory above the sm_100 per-block limit");
+  static constexpr int THREADS = 192;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t O_COL = 256;
+  // Columns of output part `part`.
+  __host__ __device__ static constexpr int part_cols(int part) {
+    return D - 256 * part < 256 ? D - 256 * part : 256;
+  }
+};
+
+// Units: (b, h, part, 256-query tile), tile fastest; one pair per unit.
+template <int D>
+inline dim3 fa_wide_pair_grid(FaParams &p, int B, int num_sms) {
+  p.nqt = (p.S + 255) / 256;
+  p.nseq = 0;
+  p.units = B * p.H * 2 * p.nqt;
+  const int pairs_max = (num_sms > 0 ? num_sms : 148) / 2;
+  return dim3(2 * (p.units < pairs_max ? p.units : pairs_max));
+}
+
+template <int D, typename OutT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    fa_wide_pair_kernel(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const FaParams p) {
+  using C = FaWide2Cfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+
+  uint8_t *sQ = smem + C::Q_OFF;
+  uint8_t *sK = smem + C::K_OFF;
+  uint8_t *sV = smem + C::V_OFF;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
+  uint64_t *q_full = bars;
+  uint64_t *q_empty = bars + 1;
+  uint64_t *k_full = bars + 2;
+  uint64_t *k_empty = k_full + C::NSTK;
+  uint64_t *v_full = k_empty + C::NSTK;
+  uint64_t *v_empty = v_full + C::NSTV;
+  uint64_t *s_full = v_empty + C::NSTV;  // [jj % 2]
+  uint64_t *p_half = s_full + 2;         // [(jj % 2) * 2 + half of the keys]
+  uint64_t *pv_done = p_half + 4;
+  uint64_t *o_full = pv_done + 1;
+  uint64_t *o_empty = o_full + 1;
+  uint64_t *drain = o_empty + 1;
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = the pair's MMA issuer
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  struct Unit {
+    int b, h, part, col0, ncols, q0, nblk;
+  };
+  auto decode = [&](int unit) {
+    Unit u;
+    const int per_bh = 2 * p.nqt;
+    const int bh = unit / per_bh;
+    const int r = unit - bh * per_bh;
+    u.part = r / p.nqt;
+    u.q0 = (r - u.part * p.nqt) * 2 * C::BM;
+    u.b = bh / p.H;
+    u.h = bh - u.b * p.H;
+    u.col0 = 256 * u.part;
+    u.ncols = C::part_cols(u.part);
+    u.nblk = (p.S_kv + C::BN - 1) / C::BN;
+    return u;
+  };
+  // Cluster address of barrier `bar` in CTA `r` (0 = the even CTA).
+  auto at = [&](uint64_t *bar, uint32_t r) { return mapa_shared(smem_u32(bar), r); };
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    for (int i = 0; i < C::NSTK; i++) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+    }
+    for (int i = 0; i < C::NSTV; i++) {
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_half[2 * b], 8);  // four softmax warps of each CTA
+      mbar_init(&p_half[2 * b + 1], 8);
+    }
+    mbar_init(pv_done, 1);
+    mbar_init(o_full, 1);
+    mbar_init(o_empty, 8);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc_pair(tmem_base_slot, C::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_base_slot;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    // Order per unit (= the MMA warp's): K_0, K_1, V_0, K_2, V_1, ...,
+    // K_{n-1}, V_{n-2}, V_{n-1}. Each CTA loads its own Q rows, its 64 keys
+    // of every K chunk and its half of the part's V columns; the bytes of
+    // both CTAs complete on the even CTA's barriers, which the even CTA arms.
+    if (lane == 0) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      bool ok = true;
+      int kpos = 0, vpos = 0, kq = 0;
+      for (int unit = pair, k = 0; unit < p.units && ok; unit += npairs, k++) {
+        const Unit un = decode(unit);
+        if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (rank == 0) mbar_arrive_expect_tx(q_full, 2 * C::Q_BYTES);
+        for (int c = 0; c < C::QCH; c++)
+          tma_load_4d_pair(sQ + c * C::ATOM, &tmQ, at(q_full, 0), c * 64,
+                           un.q0 + (int)rank * C::BM, un.h, un.b);
+        kq = k + 1;
+        const int vcols = un.ncols / 2;  // this CTA's V columns
+        for (int i = 0; i <= un.nblk && ok; i++) {
+          if (i < un.nblk) {
+            for (int c = 0; c < C::QCH; c++) {
+              const int slot = kpos % C::NSTK, round = kpos / C::NSTK;
+              if (round > 0 && !mbar_wait(&k_empty[slot], (round - 1) & 1, abort_flag)) {
+                ok = false;
+                break;
+              }
+              if (rank == 0) mbar_arrive_expect_tx(&k_full[slot], 2 * C::K_BYTES);
+              tma_load_4d_pair(sK + slot * C::K_BYTES, &tmK, at(&k_full[slot], 0), c * 64,
+                               i * C::BN + (int)rank * (C::BN / 2), un.h, un.b);
+              kpos++;
+            }
+          }
+          if (i >= 1 && ok) {
+            const int slot = vpos % C::NSTV, round = vpos / C::NSTV;
+            if (round > 0 && !mbar_wait(&v_empty[slot], (round - 1) & 1, abort_flag)) {
+              ok = false;
+              break;
+            }
+            if (rank == 0) mbar_arrive_expect_tx(&v_full[slot], 2 * vcols * C::BN * 2);
+            for (int a = 0; a < vcols / 64; a++)
+              tma_load_4d_pair(sV + slot * C::V_SLOT + a * C::ATOM, &tmV, at(&v_full[slot], 0),
+                               un.col0 + (int)rank * vcols + a * 64, (i - 1) * C::BN, un.h,
+                               un.b);
+            vpos++;
+          }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Abort path: every armed load (both CTAs' bytes) lands before exit.
+        if (kq > 0) mbar_wait_raw(q_full, (kq - 1) & 1, 100000000ull);
+        for (int u = kpos - C::NSTK < 0 ? 0 : kpos - C::NSTK; u < kpos; u++)
+          mbar_wait_raw(&k_full[u % C::NSTK], (u / C::NSTK) & 1, 100000000ull);
+        for (int u = vpos - C::NSTV < 0 ? 0 : vpos - C::NSTV; u < vpos; u++)
+          mbar_wait_raw(&v_full[u % C::NSTV], (u / C::NSTV) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------------------------------------------------- MMA issuer
+    if (rank == 0) {
+      constexpr uint32_t IDESC_S = idesc_f16_f32(2 * C::BM, C::BN, 0);
+      const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+      int kpos = 0, vpos = 0;
+      auto commit_both = [&](uint64_t *bar) {
+        if (elect_one()) {
+          mma_commit_pair(at(bar, 0));
+          mma_commit_pair(at(bar, 1));
+        }
+      };
+      auto issue_s = [&](int jj) {
+        const uint32_t dS = tmem + (uint32_t)(jj & 1) * 128;
+        for (int c = 0; c < C::QCH; c++) {
+          const int slot = kpos % C::NSTK;
+          if (!mbar_wait(&k_full[slot], (kpos / C::NSTK) & 1, abort_flag)) return false;
+          tc_fence_after();
+          const uint32_t qa = sQa + c * C::ATOM;
+          const uint32_t ka = sKa + slot * C::K_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++)
+            if (elect_one())
+              mma_ss_pair(dS, sdesc_sw128(qa + kk * 32, 16, 1024),
+                          sdesc_sw128(ka + kk * 32, 16, 1024), IDESC_S,
+                          (c > 0 || kk > 0) ? 1u : 0u);
+          commit_both(&k_empty[slot]);
+          kpos++;
+        }
+        commit_both(&s_full[jj & 1]);
+        return true;
+      };
+      // O (+)= P_jj V_jj over the part's columns: one N = ncols MMA per K=16
+      // key step (each CTA supplies ncols/2 columns as 64-column atoms).
+      auto issue_pv = [&](int jj, bool acc, uint32_t idesc_o) {
+        const int slot = vpos % C::NSTV;
+        if (!mbar_wait(&v_full[slot], (vpos / C::NSTV) & 1, abort_flag)) return false;
+        const uint32_t aP = tmem + (uint32_t)(jj & 1) * 128;
+        const uint32_t va = sVa + slot * C::V_SLOT;
+        for (int half = 0; half < 2; half++) {
+          if (!mbar_wait_cluster(&p_half[2 * (jj & 1) + half], (jj >> 1) & 1, abort_flag))
+            return false;
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < 4; kk++) {
+            const int ks = half * 4 + kk;
+            if (elect_one())
+              mma_ts_pair(tmem + C::O_COL, aP + ks * 8, sdesc_sw128(va + ks * 2048, C::ATOM, 1024),
+                          idesc_o, (acc || ks > 0) ? 1u : 0u);
+          }
+        }
+        commit_both(&v_empty[slot]);
+        vpos++;
+        return true;
+      };
+      bool ok = true;
+      int jb = 0;
+      for (int unit = pair, k = 0; unit < p.units && ok; unit += npairs, k++) {
+        const Unit un = decode(unit);
+        const int nblk = un.nblk;
+        const uint32_t idesc_o = idesc_f16_f32(2 * C::BM, (uint32_t)un.ncols, 1);
+        if (!(ok = mbar_wait(q_full, k & 1, abort_flag))) break;
+        tc_fence_after();
+        if (!(ok = issue_s(jb))) break;
+        if (nblk > 1 && !(ok = issue_s(jb + 1))) break;
+        if (nblk <= 2) commit_both(q_empty);
+        for (int j = 0; j < nblk; j++) {
+          const int jj = jb + j;
+          if (j == 0 && k > 0 && !(ok = mbar_wait_cluster(o_empty, (k - 1) & 1, abort_flag)))
+            break;
+          if (!(ok = issue_pv(jj, j > 0, idesc_o))) break;
+          commit_both(pv_done);
+          if (j + 2 < nblk) {
+            if (!(ok = issue_s(jj + 2))) break;
+            if (j + 3 == nblk) commit_both(q_empty);
+          }
+        }
+        if (!ok) break;
+        commit_both(o_full);
+        jb += nblk;
+      }
+      if (elect_one()) mma_commit_pair(smem_u32(drain));
+      mbar_wait_raw(drain, 0, 100000000ull);
+    }
+  } else {
+    // ------------------------------------------------------------- softmax
+    const int row = threadIdx.x;  // 0..127 = TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t tO = tmem + lane_off + C::O_COL;
+    const float sl2 = p.scale_log2;
+    bool ok = true;
+    int jb = 0;
+    for (int unit = pair, k = 0; unit < p.units && ok; unit += npairs, k++) {
+      const Unit un = decode(unit);
+      const int nblk = un.nblk;
+      float m_used = -INFINITY;
+      float l = 0.0f;
+      for (int j = 0; j < nblk; j++) {
+        const int jj = jb + j;
+        const uint32_t tS = tmem + lane_off + (uint32_t)(jj & 1) * 128;
+        ok = __all_sync(0xffffffffu, mbar_wait(&s_full[jj & 1], (jj >> 1) & 1, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        const int valid = p.S_kv - j * C::BN;
+        uint32_t sbuf[128];
+#pragma unroll
+        for (int c = 0; c < 4; c++) tmem_ld32(tS + c * 32, sbuf + c * 32);
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; c++) reg_fence32(sbuf + c * 32);
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          float *v = reinterpret_cast<float *>(sbuf + c * 32);
+          if (valid < C::BN) {
+#pragma unroll
+            for (int i = 0; i < 32; i++)
+              if (c * 32 + i >= valid) v[i] = -INFINITY;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) mx[(i >> 1) & 3] = max3f(mx[(i >> 1) & 3], v[i], v[i + 1]);
+        }
+        const float m_new = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sl2;
+        const bool need = m_new > m_used + kMaxExp;
+        if (jj > 0) {
+          ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (jj - 1) & 1, abort_flag));
+          if (!ok) break;
+        }
+        if (__any_sync(0xffffffffu, need)) {
+          const float m_tgt = need ? m_new : m_used;
+          const float factor = ex2_approx(m_used - m_tgt);
+          l *= factor;
+          if (j > 0) {
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < un.ncols / 32; c++) {
+              uint32_t o[32];
+              tmem_ld32(tO + c * 32, o);
+              tmem_wait_ld();
+              reg_fence32(o);
+#pragma unroll
+              for (int i = 0; i < 32; i++) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+              tmem_st32(tO + c * 32, o);
+            }
+          }
+          m_used = m_tgt;
+        }
+        uint64_t part2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+        const uint64_t sl2x2 = f2_pack(sl2, sl2);
+        const uint64_t neg_mx2 = f2_pack(-m_used, -m_used);
+#pragma unroll
+        for (int c = 0; c < 4; c++) {
+          const float *v = reinterpret_cast<const float *>(sbuf + c * 32);
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; i++) {
+            const float2 x = f2_unpack(f2_fma(f2_pack(v[2 * i], v[2 * i + 1]), sl2x2, neg_mx2));
+            uint64_t pp;
+            if ((kExp2EmuMask >> i) & 1u)
+              pp = exp2_poly_x2(f2_pack(fmaxf(x.x, -125.0f), fmaxf(x.y, -125.0f)));
+            else
+              pp = f2_pack(ex2_approx(x.x), ex2_approx(x.y));
+            part2[i & 1] = f2_add(part2[i & 1], pp);
+            const float2 pf = f2_unpack(pp);
+            pk[i] = pack_f16x2(pf.x, pf.y);
+          }
+          tmem_st16(tS + c * 16, pk);
+          if (c == 1 || c == 3) {
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_remote(at(&p_half[2 * (jj & 1) + (c >> 1)], 0));
+          }
+        }
+        const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
+        l += (s0.x + s0.y) + (s1.x + s1.y);
+      }
+      jb += nblk;
+      if (!ok) break;
+      // ------------------------------------------------------- epilogue
+      ok = __all_sync(0xffffffffu, mbar_wait(o_full, k & 1, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      const int q = un.q0 + (int)rank * C::BM + row;
+      const bool qin = q < p.S;
+      OutT *dst = reinterpret_cast<OutT *>(p.o) + (long long)un.b * p.o_batch_stride +
+                  (long long)q * p.o_row_stride + (long long)un.h * D + un.col0;
+      const float inv_l = 1.0f / l;
+      const int nc = un.ncols / 32;
+#pragma unroll 1
+      for (int c = 0; c < nc; c++) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_wait_ld();
+        reg_fence32(o);
+        if (c == nc - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_remote(at(o_empty, 0));
+        }
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[i]) * inv_l;
+        if (qin) store_row_chunk<OutT>(dst + c * 32, v);
+      }
+      if (p.lse != nullptr && qin && un.part == 0)
+        p.lse[((long long)un.b * p.H + un.h) * p.S + q] =
+            (m_used + log2f(l)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no pair MMA, remote arrival or peer TMA write is left in flight
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
+}
+
 }  // namespace llmr

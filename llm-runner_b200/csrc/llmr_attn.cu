@@ -92,10 +92,10 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 4-D fp16 tensor map over (d, s, h, b) with a 64 x 128 x 1 x 1 box and
+// 4-D fp16 tensor map over (d, s, h, b) with a 64 x box_rows x 1 x 1 box and
 // 128-byte swizzle: one box is one SW128 K-major operand chunk.
 int make_map(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S,
-             int H, int B, long long rs, long long hs, long long bs) {
+             int H, int B, long long rs, long long hs, long long bs, int box_rows = 128) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((rs * 2) & 15) || ((hs * 2) & 15) ||
@@ -103,7 +103,7 @@ int make_map(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S,
     return fail(ctx, LLMR_EINVAL, "TMA operand base/strides must be 16-byte aligned");
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)rs * 2, (cuuint64_t)hs * 2, (cuuint64_t)bs * 2};
-  cuuint32_t box[4] = {64, 128, 1, 1};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -382,19 +382,66 @@ int launch_fa_wide(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   return after_launch(ctx, "fa_wide_tc");
 }
 
-int launch_fa_wide_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
+template <int D, typename OutT>
+int launch_fa_wide_pair(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
+                        const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale,
+                        void *o, long long o_rs, long long o_bs, float *lse) {
+  using C = FaWide2Cfg<D>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    if (smem_optin(ctx) < C::SMEM_BYTES)
+      return fail(ctx, LLMR_ECUDA, "fa_wide_pair needs %d bytes of shared memory per block",
+                  C::SMEM_BYTES);
+    CUDA_TRY(ctx, cudaFuncSetAttribute(fa_wide_pair_kernel<D, OutT>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       C::SMEM_BYTES));
+    attr_set = true;
+  }
+  FaParams p;
+  memset(&p, 0, sizeof p);
+  p.S = S;
+  p.S_kv = S_kv;
+  p.H = H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.o = o;
+  p.o_row_stride = o_rs;
+  p.o_batch_stride = o_bs;
+  p.lse = lse;
+  p.err = ctx->d_err;
+  const dim3 grid = fa_wide_pair_grid<D>(p, B, ctx->num_sms);
+  fa_wide_pair_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
+  return after_launch(ctx, "fa_wide_pair");
+}
+
+// The pair kernel is the default; LLMR_WIDE_SINGLE_CTA selects the
+// single-CTA kernel.
+bool wide_single_cta() { return getenv("LLMR_WIDE_SINGLE_CTA") != nullptr; }
+
+// single: the single-CTA kernel (mk with 128-row boxes like mq and mv), else
+// the pair kernel (mk with 64-row boxes: each CTA loads 64 keys per block).
+int launch_fa_wide_any(llmr_ctx *ctx, bool single, int D, llmr_dtype od, const CUtensorMap &mq,
                        const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S,
                        int S_kv, float scale, void *o, long long o_rs, long long o_bs,
                        float *lse) {
 #define LLMR_WIDE_ARGS ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse
-  if (D == 512) {
-    if (od == LLMR_F32) return launch_fa_wide<512, float>(LLMR_WIDE_ARGS);
-    if (od == LLMR_F16) return launch_fa_wide<512, __half>(LLMR_WIDE_ARGS);
-    return launch_fa_wide<512, __nv_bfloat16>(LLMR_WIDE_ARGS);
+  if (single) {
+    if (D == 512) {
+      if (od == LLMR_F32) return launch_fa_wide<512, float>(LLMR_WIDE_ARGS);
+      if (od == LLMR_F16) return launch_fa_wide<512, __half>(LLMR_WIDE_ARGS);
+      return launch_fa_wide<512, __nv_bfloat16>(LLMR_WIDE_ARGS);
+    }
+    if (od == LLMR_F32) return launch_fa_wide<384, float>(LLMR_WIDE_ARGS);
+    if (od == LLMR_F16) return launch_fa_wide<384, __half>(LLMR_WIDE_ARGS);
+    return launch_fa_wide<384, __nv_bfloat16>(LLMR_WIDE_ARGS);
   }
-  if (od == LLMR_F32) return launch_fa_wide<384, float>(LLMR_WIDE_ARGS);
-  if (od == LLMR_F16) return launch_fa_wide<384, __half>(LLMR_WIDE_ARGS);
-  return launch_fa_wide<384, __nv_bfloat16>(LLMR_WIDE_ARGS);
+  if (D == 512) {
+    if (od == LLMR_F32) return launch_fa_wide_pair<512, float>(LLMR_WIDE_ARGS);
+    if (od == LLMR_F16) return launch_fa_wide_pair<512, __half>(LLMR_WIDE_ARGS);
+    return launch_fa_wide_pair<512, __nv_bfloat16>(LLMR_WIDE_ARGS);
+  }
+  if (od == LLMR_F32) return launch_fa_wide_pair<384, float>(LLMR_WIDE_ARGS);
+  if (od == LLMR_F16) return launch_fa_wide_pair<384, __half>(LLMR_WIDE_ARGS);
+  return launch_fa_wide_pair<384, __nv_bfloat16>(LLMR_WIDE_ARGS);
 #undef LLMR_WIDE_ARGS
 }
 
@@ -893,9 +940,12 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
 
   CUtensorMap mq, mk, mv;
   const bool direct = need == 0;
+  // The wide pair kernel loads 64 keys per CTA and block.
+  const bool wide_single = wide && wide_single_cta();
+  const int k_box = wide && !wide_single ? 64 : 128;
   if (direct) {
     if ((rc = make_map(ctx, &mq, q, D, S, H, B, qs[1], qs[2], qs[0]))) return rc;
-    if ((rc = make_map(ctx, &mk, k, D, S_kv, H, B, ks[1], ks[2], ks[0]))) return rc;
+    if ((rc = make_map(ctx, &mk, k, D, S_kv, H, B, ks[1], ks[2], ks[0], k_box))) return rc;
     if ((rc = make_map(ctx, &mv, v, D, S_kv, H, B, vs[1], vs[2], vs[0]))) return rc;
   } else {
     __half *w = static_cast<__half *>(ctx->ws);
@@ -905,13 +955,13 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     // Workspace layout: dense [3][B][H][S][D] fp16.
     const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
     if ((rc = make_map(ctx, &mq, w, D, S, H, B, rs, hs, bs))) return rc;
-    if ((rc = make_map(ctx, &mk, w + plane, D, S, H, B, rs, hs, bs))) return rc;
+    if ((rc = make_map(ctx, &mk, w + plane, D, S, H, B, rs, hs, bs, k_box))) return rc;
     if ((rc = make_map(ctx, &mv, w + 2 * plane, D, S, H, B, rs, hs, bs))) return rc;
   }
   mark(1);
   if (wide)
-    rc = launch_fa_wide_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
-                            o_bs, lse_out);
+    rc = launch_fa_wide_any(ctx, wide_single, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv,
+                            d->scale, o, o_rs, o_bs, lse_out);
   else
     rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
                           o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0, nseq, seq_off);

@@ -197,6 +197,17 @@ __device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorM
       "l"(map), "r"(mbar_cluster_addr), "r"(c0), "r"(c1)
       : "memory");
 }
+// 4-D tiled load into this CTA's shared memory whose completion counts on an
+// mbarrier of either CTA of the pair (cluster address); no multicast.
+__device__ __forceinline__ void tma_load_4d_pair(void *smem_dst, const CUtensorMap *map,
+                                                 uint32_t mbar_cluster_addr, int c0, int c1,
+                                                 int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::"
+      "bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(map), "r"(mbar_cluster_addr), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t *dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                    smem_u32(dst_smem)),
@@ -219,6 +230,17 @@ __device__ __forceinline__ void mma_ss_pair(uint32_t d_tmem, uint64_t adesc, uin
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// D[tmem of both CTAs] (+)= A[tmem of both CTAs, each its own rows] * B[smem,
+// N split over the pair]; issued by one thread of the even CTA.
+__device__ __forceinline__ void mma_ts_pair(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // Arrive once on the mbarrier at cluster address `bar` (either CTA) when the

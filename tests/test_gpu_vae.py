@@ -51,6 +51,23 @@ def test_vae_attention_mirror_vs_oracle(ctx, S, H, D):
     _check(o.cpu().numpy(), want, 2e-3, 2e-4)
 
 
+@pytest.mark.parametrize("S,D", [(300, 512), (129, 384)])
+def test_vae_single_cta_kernel(ctx, monkeypatch, S, D):
+    """The single-CTA wide kernel (LLMR_WIDE_SINGLE_CTA; the default is the
+    CTA-pair kernel) on ragged cases."""
+    import llmr_attn as L
+    torch = _t()
+    monkeypatch.setenv("LLMR_WIDE_SINGLE_CTA", "1")
+    q, k, v = _inputs(S + D, S, D)
+    want = O.vae_attention(q, k, v, D, 1, S, D ** -0.5)
+    o = torch.empty((S, D), device="cuda")
+    ctx.reserve(3 * S * D * 2)
+    L.vae_attention(ctx, *(torch.from_numpy(a).cuda() for a in (q, k, v)), o, D, 1, S,
+                    D ** -0.5)
+    ctx.sync()
+    _check(o.cpu().numpy(), want, 2e-3, 2e-4)
+
+
 def test_vae_attention_channels_stride(ctx):
     """channels > n_heads * head_dim: rows of [S, C] with padding columns,
     which the op neither reads into the result nor writes."""
@@ -70,9 +87,9 @@ def test_vae_attention_channels_stride(ctx):
 
 
 def test_vae_attention_many_units_per_cta(ctx):
-    """10240 queries x 2 output halves = 160 units > 148 SMs: CTAs walk more
-    than one unit (Q reload, O hand-over between units). Checked on the first
-    and last query tiles."""
+    """10240 queries: 40 tiles of 256 x 2 output parts = 80 units > 74 CTA
+    pairs, so pairs walk more than one unit (Q reload, O hand-over between
+    units). Checked on the first and last query tiles."""
     import llmr_attn as L
     torch = _t()
     S, D = 10240, 512
