@@ -8,6 +8,7 @@ written separately from oracle/attn_oracle.cpp, from the same shader sources:
   dependencies/zimage.c3l/shaders/zimage.slang:575-601, :623-659
   dependencies/zimage.c3l/shaders/mrope.slang:33-54
   lib/shaders/diffusion.slang:478-569                        (spatial_attention)
+  lib/shaders/diffusion.slang:1846-1975                      (vae_attention)
   dependencies/depth_anything.c3l/shaders/depth.slang:40-58  (split_qkv)
   dependencies/flux.c3l/flux_dit.c3:461-497                  (RoPE tables)
 Two restatements agreeing is what the oracle is checked against.
@@ -161,6 +162,50 @@ def np_spatial(Q, K, V, D, H, S, scale):
     return O
 
 
+def np_vae(Q, K, V, D, H, S, scale):
+    """diffusion.slang:1846-1975 on [S, H*D] (head h at columns h*D..): keys in
+    4096-key tiles with a running max / sum; per tile the scores are
+    (q . k) * scale summed over d in order, the max and the exponential sum
+    are 256 lane partials (lane g takes keys g, g+256, ...) folded by a
+    halving tree, and the output gains sum_i p_i v_i over i in order after a
+    rescale by exp(old_max - new_max). All queries of a head at once."""
+    TILE = 4096
+    O = np.zeros((S, H * D), f32)
+    for h in range(H):
+        q = Q[:, h * D:(h + 1) * D]
+        k = K[:, h * D:(h + 1) * D]
+        v = V[:, h * D:(h + 1) * D]
+        acc = np.zeros((S, D), f32)
+        run_max = np.full((S, 1), -1.0e30, f32)
+        run_sum = np.zeros((S, 1), f32)
+        for t0 in range(0, S, TILE):
+            n = min(TILE, S - t0)
+            dot = np.zeros((S, n), f32)
+            for d in range(D):
+                dot = dot + q[:, d:d + 1] * k[t0:t0 + n, d][None, :]
+            sc = dot * f32(scale)
+            tmax = sc.max(axis=1, keepdims=True)
+            new_max = np.maximum(run_max, tmax)
+            alpha = np.exp(run_max - new_max, dtype=f32)
+            ev = np.exp(sc - new_max, dtype=f32)
+            part = np.zeros((S, 256), f32)
+            for c0 in range(0, n, 256):
+                m = min(256, n - c0)
+                part[:, :m] = part[:, :m] + ev[:, c0:c0 + m]
+            w = 128
+            while w > 0:
+                part[:, :w] = part[:, :w] + part[:, w:2 * w]
+                w //= 2
+            vacc = np.zeros((S, D), f32)
+            for i in range(n):
+                vacc = vacc + ev[:, i:i + 1] * v[t0 + i][None, :]
+            acc = acc * alpha + vacc
+            run_sum = run_sum * alpha + part[:, :1]
+            run_max = new_max
+        O[:, h * D:(h + 1) * D] = acc * (f32(1.0) / run_sum)
+    return O
+
+
 def main():
     rng = np.random.default_rng(23)
     man = {}
@@ -260,6 +305,16 @@ def main():
                          "sin": save("block_sin", s),
                          "out": save("block_out", np_fa2(qt, kt, vt, D, H, S,
                                                          f32(1.0 / np.sqrt(128.0))))}
+
+    # vae_attention: [S, H*D], two heads, S = 4100 crosses the 4096-key tile
+    S, H, D = 4100, 2, 4
+    q = rng.standard_normal((S, H * D), dtype=f32)
+    k = rng.standard_normal((S, H * D), dtype=f32)
+    v = rng.standard_normal((S, H * D), dtype=f32)
+    sc = f32(0.5)
+    man["vae"] = {"params": {"S": S, "H": H, "D": D, "scale": float(sc)},
+                  "q": save("vae_q", q), "k": save("vae_k", k), "v": save("vae_v", v),
+                  "out": save("vae_out", np_vae(q, k, v, D, H, S, sc))}
 
     with open(os.path.join(HERE, "manifest.json"), "w") as fh:
         json.dump(man, fh, indent=1, sort_keys=True)

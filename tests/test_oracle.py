@@ -91,6 +91,32 @@ def test_spatial_golden(manifest):
     np.testing.assert_allclose(got, load_golden(m["out"]), rtol=0, atol=2e-6)
 
 
+def test_vae_golden(manifest):
+    """orc_vae_attention against the independent numpy restatement of
+    vae_attention (two heads in [S, C], 4100 keys across the shader's
+    4096-key tile boundary)."""
+    m = manifest["vae"]
+    p = m["params"]
+    got = O.vae_attention(load_golden(m["q"]), load_golden(m["k"]), load_golden(m["v"]),
+                          p["D"], p["H"], p["S"], p["scale"])
+    np.testing.assert_allclose(got, load_golden(m["out"]), rtol=0, atol=2e-6)
+
+
+def test_vae_is_exact_fp32_and_row_subsets():
+    """The shader's tiled fp32 softmax agrees with fp64 attention within 1e-5
+    at D = 512, and a row range computes exactly those rows."""
+    rng = np.random.default_rng(14)
+    S, D = 150, 512
+    q, k, v = (rng.standard_normal((S, D), dtype=np.float32) for _ in range(3))
+    sc = D ** -0.5
+    out = O.vae_attention(q, k, v, D, 1, S, sc)
+    ex = O.attention_f64(q[None], k[None], v[None], D, 1, S, sc)[0]
+    assert np.abs(out - ex).max() < 1e-5
+    part = O.vae_attention(q, k, v, D, 1, S, sc, rows=(40, 90))
+    np.testing.assert_array_equal(part[40:90], out[40:90])
+    assert np.all(part[:40] == 0) and np.all(part[90:] == 0)
+
+
 def test_split_qkv_golden(manifest):
     m = manifest["split_qkv"]
     p = m["params"]
