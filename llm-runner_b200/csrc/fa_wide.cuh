@@ -15,6 +15,11 @@
 // they use the same row max and row sum. QK^T is thereby done twice: the MMA
 // work is 1.5x the algorithmic FLOPs.
 //
+// Two kernels: fa_wide_pair_kernel (further down; the default) runs the units
+// on 2-CTA clusters with cta_group::2 MMAs, so that each CTA loads half of
+// every shared operand; fa_wide_tc_kernel (here; LLMR_WIDE_SINGLE_CTA) is
+// the single-CTA form of the same schedule:
+//
 // CTA = 128 query rows x one output half; 192 threads:
 //   warps 0-3  softmax (thread i owns query row i = TMEM lane i)
 //   warp  4    TMA producer: Q once per unit (resident, D/64 chunks), then
