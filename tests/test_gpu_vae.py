@@ -160,6 +160,30 @@ def test_wide_fused_dtypes_layouts_lse(ctx, in_dt, out_dt, layout):
     assert np.abs(lse.cpu().numpy() - want_lse).max() <= 1e-3
 
 
+@pytest.mark.parametrize("single", [False, True])
+def test_wide_kv_len_differs_from_queries(ctx, monkeypatch, single):
+    """kv_seq_len at D = 512: 200 queries over 333 keys (fp16 BHSD read in
+    place), both wide kernels, against a float64 restatement."""
+    import llmr_attn as L
+    torch = _t()
+    if single:
+        monkeypatch.setenv("LLMR_WIDE_SINGLE_CTA", "1")
+    rng = np.random.default_rng(9)
+    S, T, D = 200, 333, 512
+    q = rng.standard_normal((S, D)).astype(np.float16)
+    k = rng.standard_normal((T, D)).astype(np.float16)
+    v = rng.standard_normal((T, D)).astype(np.float16)
+    cfg = L.AttnConfig(n_heads=1, head_dim=D, scale=D ** -0.5, layout=L.BHSD)
+    o = torch.empty((1, S, D), device="cuda")
+    L.attention_fused(ctx, *(torch.from_numpy(a)[None, None].cuda() for a in (q, k, v)), o, cfg,
+                      batch=1, seq_len=S, kv_len=T)
+    ctx.sync()
+    s = q.astype(np.float64) @ k.astype(np.float64).T * D ** -0.5
+    p = np.exp(s - s.max(-1, keepdims=True))
+    want = (p / p.sum(-1, keepdims=True)) @ v.astype(np.float64)
+    _check(o[0].cpu().numpy(), want, 2e-3, 2e-4)
+
+
 def test_wide_rejects(ctx):
     import llmr_attn as L
     torch = _t()
