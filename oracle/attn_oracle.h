@@ -11,7 +11,9 @@
  * (it needs the C3 compiler, the Slang compiler and a Vulkan device). Each
  * function below is a line-by-line restatement of a reference shader or host
  * routine, cited by file:line inside the reference project, cross-checked
- * against an independent numpy restatement (tests/golden/make_golden.py).
+ * against an independent numpy restatement (tests/golden/make_golden.py) and,
+ * for the attention math, against a restatement of the reference test
+ * suite's own CPU attention (test/mesh_encoder_test.c3:95-135).
  *
  * All buffers are fp32, as the reference's RWStructuredBuffer<float> bindings.
  */

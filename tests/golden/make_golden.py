@@ -9,6 +9,8 @@ written separately from oracle/attn_oracle.cpp, from the same shader sources:
   dependencies/zimage.c3l/shaders/mrope.slang:33-54
   lib/shaders/diffusion.slang:478-569                        (spatial_attention)
   lib/shaders/diffusion.slang:1846-1975                      (vae_attention)
+  test/mesh_encoder_test.c3:95-135       (cpu_attention, the reference's own
+                                          CPU check of its FA2-style kernel)
   dependencies/depth_anything.c3l/shaders/depth.slang:40-58  (split_qkv)
   dependencies/flux.c3l/flux_dit.c3:461-497                  (RoPE tables)
 Two restatements agreeing is what the oracle is checked against.
@@ -159,6 +161,27 @@ def np_spatial(Q, K, V, D, H, S, scale):
             for pos in range(S):
                 acc = acc + p[pos] * V[h, pos]
             O[h, qp] = acc
+    return O
+
+
+def np_cpu_attention(Q, K, V, D, H, S, scale):
+    """The reference test suite's CPU attention (test/mesh_encoder_test.c3:
+    95-135) on [H, S, D]: fp32 dot products summed over d in order, scores
+    scaled, the row max, exp(s - max), the total summed over keys in order,
+    and out = (sum_s p_s v_s, s in order) / total. All queries at once."""
+    O = np.zeros((H, S, D), f32)
+    for h in range(H):
+        dot = np.zeros((S, S), f32)
+        for d in range(D):
+            dot = dot + Q[h, :, d][:, None] * K[h, :, d][None, :]
+        sc = dot * f32(scale)
+        top = sc.max(axis=1, keepdims=True)
+        e = np.exp(sc - top, dtype=f32)
+        total = np.add.accumulate(e, axis=1, dtype=f32)[:, -1:]
+        acc = np.zeros((S, D), f32)
+        for k in range(S):
+            acc = acc + e[:, k:k + 1] * V[h, k][None, :]
+        O[h] = acc / total
     return O
 
 
@@ -315,6 +338,18 @@ def main():
     man["vae"] = {"params": {"S": S, "H": H, "D": D, "scale": float(sc)},
                   "q": save("vae_q", q), "k": save("vae_k", k), "v": save("vae_v", v),
                   "out": save("vae_out", np_vae(q, k, v, D, H, S, sc))}
+
+    # The reference test's cpu_attention on the spatial_attention and
+    # flash_attention_v2 fixtures' inputs (no new random draws).
+    for key in ("spatial", "fa2"):
+        m = man[key]
+        p = m["params"]
+        ins = [np.fromfile(os.path.join(HERE, m[t]["file"]), dtype=f32, offset=16).reshape(
+            m[t]["shape"]) for t in ("q", "k", "v")]
+        man["cpu_attention_" + key] = {
+            "params": p, "inputs_of": key,
+            "out": save("cpu_attention_" + key + "_out",
+                        np_cpu_attention(*ins, p["D"], p["H"], p["S"], f32(p["scale"])))}
 
     with open(os.path.join(HERE, "manifest.json"), "w") as fh:
         json.dump(man, fh, indent=1, sort_keys=True)

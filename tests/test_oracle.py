@@ -117,6 +117,32 @@ def test_vae_is_exact_fp32_and_row_subsets():
     assert np.all(part[:40] == 0) and np.all(part[90:] == 0)
 
 
+def test_exact_path_matches_reference_test_cpu_attention(manifest):
+    """The reference's own CPU attention (test/mesh_encoder_test.c3:95-135,
+    restated in tests/golden/make_golden.py) on the spatial fixture's inputs
+    equals the oracle's spatial_attention to fp32 rounding."""
+    m = manifest["spatial"]
+    p = m["params"]
+    got = O.spatial_attention(load_golden(m["q"]), load_golden(m["k"]), load_golden(m["v"]),
+                              p["D"], p["H"], p["S"], p["scale"])
+    want = load_golden(manifest["cpu_attention_spatial"]["out"])
+    np.testing.assert_allclose(got, want, rtol=0, atol=1e-6)
+
+
+def test_fa2_within_reference_test_tolerance(manifest):
+    """The oracle's flash_attention_v2 (fp16 operands) stays within the
+    tolerance the reference's own test gives its FA2-style shader against
+    cpu_attention (expect_close(..., 1e-3f), test/mesh_encoder_test.c3:322,
+    :361) on the fa2 fixture's inputs (ragged S = 45, D = 128)."""
+    m = manifest["fa2"]
+    p = m["params"]
+    got = O.flash_attention_v2(load_golden(m["q"]), load_golden(m["k"]), load_golden(m["v"]),
+                               p["D"], p["H"], p["S"], p["scale"])
+    want = load_golden(manifest["cpu_attention_fa2"]["out"])
+    want = want.transpose(1, 0, 2).reshape(p["S"], p["H"] * p["D"])
+    assert np.abs(got - want).max() <= 1e-3
+
+
 def test_split_qkv_golden(manifest):
     m = manifest["split_qkv"]
     p = m["params"]
