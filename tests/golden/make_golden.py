@@ -11,6 +11,7 @@ written separately from oracle/attn_oracle.cpp, from the same shader sources:
   lib/shaders/diffusion.slang:1846-1975                      (vae_attention)
   test/mesh_encoder_test.c3:95-135       (cpu_attention, the reference's own
                                           CPU check of its FA2-style kernel)
+  test/mesh_encoder_test.c3:81-92        (cpu_rmsnorm)
   dependencies/depth_anything.c3l/shaders/depth.slang:40-58  (split_qkv)
   dependencies/flux.c3l/flux_dit.c3:461-497                  (RoPE tables)
 Two restatements agreeing is what the oracle is checked against.
@@ -185,6 +186,16 @@ def np_cpu_attention(Q, K, V, D, H, S, scale):
     return O
 
 
+def np_cpu_rmsnorm(x, w, rows, dim, eps):
+    """The reference test suite's CPU RMSNorm (test/mesh_encoder_test.c3:81-92):
+    squares summed in order, inv_rms = 1 / sqrt(squares / dim + eps),
+    out = x * inv_rms * w."""
+    x = x.reshape(rows, dim)
+    sq = np.add.accumulate(x * x, axis=1, dtype=f32)[:, -1:]
+    inv = f32(1.0) / np.sqrt(sq / f32(dim) + f32(eps), dtype=f32)
+    return (x * inv * w[None, :]).astype(f32)
+
+
 def np_vae(Q, K, V, D, H, S, scale):
     """diffusion.slang:1846-1975 on [S, H*D] (head h at columns h*D..): keys in
     4096-key tiles with a running max / sum; per tile the scores are
@@ -350,6 +361,18 @@ def main():
             "params": p, "inputs_of": key,
             "out": save("cpu_attention_" + key + "_out",
                         np_cpu_attention(*ins, p["D"], p["H"], p["S"], f32(p["scale"])))}
+
+    # The reference test's cpu_rmsnorm on the head_norm fixture: rows are
+    # (token, head) pairs of D elements.
+    m = man["head_norm"]
+    p = m["params"]
+    x = np.fromfile(os.path.join(HERE, m["x"]["file"]), dtype=f32, offset=16)
+    g = np.fromfile(os.path.join(HERE, m["gain"]["file"]), dtype=f32, offset=16)
+    man["cpu_rmsnorm_head_norm"] = {
+        "params": p, "inputs_of": "head_norm",
+        "out": save("cpu_rmsnorm_head_norm_out",
+                    np_cpu_rmsnorm(x, g, p["S"] * p["H"], p["D"], p["eps"]).reshape(
+                        p["S"], p["H"] * p["D"]))}
 
     with open(os.path.join(HERE, "manifest.json"), "w") as fh:
         json.dump(man, fh, indent=1, sort_keys=True)

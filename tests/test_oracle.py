@@ -41,6 +41,19 @@ def test_head_norm_golden(manifest):
     np.testing.assert_allclose(x, load_golden(m["out"]), rtol=0, atol=2e-6)
 
 
+def test_head_norm_matches_reference_test_cpu_rmsnorm(manifest):
+    """batch_head_norm equals the reference test suite's own CPU RMSNorm
+    (test/mesh_encoder_test.c3:81-92, restated in the fixture generator) per
+    (token, head) row, to fp32 rounding (the shader sums the squares as a
+    256-lane tree, the test in order)."""
+    m = manifest["head_norm"]
+    p = m["params"]
+    x = load_golden(m["x"])
+    O.batch_head_norm(x, load_golden(m["gain"]), p["H"], p["D"], p["S"], p["eps"])
+    want = load_golden(manifest["cpu_rmsnorm_head_norm"]["out"])
+    np.testing.assert_allclose(x, want, rtol=0, atol=2e-6)
+
+
 @pytest.mark.parametrize("direction", [0, 1])
 def test_transpose_golden(manifest, direction):
     m = manifest["transpose"]
