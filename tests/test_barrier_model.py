@@ -1,6 +1,7 @@
-"""CPU: randomised models of the wide-head attention kernels' mbarrier
-protocols (llm-runner_b200/csrc/fa_wide.cuh), the model the kernels were
-checked against before their first GPU run.
+"""CPU: randomised models of the attention kernels' mbarrier protocols —
+fa_fwd_tc_kernel (llm-runner_b200/csrc/fa_tc.cuh) and the two wide-head
+kernels (fa_wide.cuh, checked against these models before their first GPU
+run).
 
 Each model runs the kernel's roles as coroutines under a random scheduler
 with random stalls: the TMA producer(s), the MMA-issuing warp, the softmax
@@ -594,6 +595,202 @@ def run_pair(seed, QCH, NSTK, NSTV, nblk, units, p_rescale, odd_waits_its_slots=
 
 
 
+def run_fa128(seed, NST, nblk, units, p_rescale, pv_first=True):
+    """fa_fwd_tc_kernel (fa_tc.cuh): two query tiles per unit, one S buffer
+    per tile, K_j / V_j through an NST-slot ring, MMA order S0(0), S1(0),
+    then per block PV0(j) (two halves), S0(j+1), PV1(j), S1(j+1). The
+    softmax rescales O without waiting for P.V: S_t(j) is issued after
+    PV_t(j-1), so seeing S_t(j) complete implies PV_t(j-1) has.
+    pv_first=False plants a bug: tile 0's next S issued before its P.V."""
+    rng = random.Random(seed)
+    q_full, q_empty = Bar("q_full", 1), Bar("q_empty", 1)
+    kv_full = [Bar(f"kv_full{i}", 1) for i in range(NST)]
+    kv_empty = [Bar(f"kv_empty{i}", 1) for i in range(NST)]
+    s_full = [Bar(f"s_full{t}", 1) for t in range(2)]
+    p_half = [Bar(f"p_half{i}", 4) for i in range(4)]
+    o_full = [Bar(f"o_full{t}", 1) for t in range(2)]
+    o_empty = [Bar(f"o_empty{t}", 4) for t in range(2)]
+    slot_tag, slot_uses = [None] * NST, [0] * NST
+    q_tag, s_done = [None], {}
+    tma_q, mma_q = [], []
+    sbuf = [[None] * 4 for _ in range(2)]        # per tile, per warp: ("S"|"P", jj, halves)
+    o_last = [None, None]                          # (jj, half) of the last PV per tile
+    epi = set()
+
+    def producer():
+        u = 0
+        for k in range(units):
+            if k > 0:
+                yield from wait(q_empty, k - 1)
+            tma_q.append(("Q", k, None, q_full))
+            yield True
+            for j in range(nblk):
+                for kind in ("K", "V"):
+                    slot, rnd = u % NST, u // NST
+                    if rnd > 0:
+                        yield from wait(kv_empty[slot], rnd - 1)
+                    tma_q.append((kind, (k, j), slot, kv_full[slot]))
+                    u += 1
+                    yield True
+
+    def mma():
+        jb = 0
+        for k in range(units):
+            ub = 2 * jb
+            yield from wait(q_full, k)
+            yield from wait(kv_full[ub % NST], ub // NST)
+            for t in range(2):
+                mma_q.append(("S", (t, jb, ub % NST, k, 0)))
+                mma_q.append(("commit", s_full[t]))
+            mma_q.append(("commit", kv_empty[ub % NST]))
+            if nblk == 1:
+                mma_q.append(("commit", q_empty))
+            yield True
+            for j in range(nblk):
+                jj = jb + j
+                uV, uK = 2 * jj + 1, 2 * jj + 2
+                more = j + 1 < nblk
+                yield from wait(kv_full[uV % NST], uV // NST)
+                for t in range(2):
+                    if j == 0 and k > 0:
+                        yield from wait(o_empty[t], k - 1)
+                    early = t == 0 and more and not pv_first
+                    if early:
+                        yield from wait(kv_full[uK % NST], uK // NST)
+                        mma_q.append(("S", (0, jj + 1, uK % NST, k, j + 1)))
+                        mma_q.append(("commit", s_full[0]))
+                    for half in range(2):
+                        yield from wait(p_half[2 * t + half], jj)
+                        mma_q.append(("PV", (t, jj, half, uV % NST, k, j)))
+                    if t == 0:
+                        if more and not early:
+                            yield from wait(kv_full[uK % NST], uK // NST)
+                            mma_q.append(("S", (0, jj + 1, uK % NST, k, j + 1)))
+                            mma_q.append(("commit", s_full[0]))
+                        elif not more:
+                            mma_q.append(("commit", o_full[0]))
+                    else:
+                        mma_q.append(("commit", kv_empty[uV % NST]))
+                        if more:
+                            mma_q.append(("S", (1, jj + 1, uK % NST, k, j + 1)))
+                            mma_q.append(("commit", s_full[1]))
+                            mma_q.append(("commit", kv_empty[uK % NST]))
+                            if j + 2 == nblk:
+                                mma_q.append(("commit", q_empty))
+                        else:
+                            mma_q.append(("commit", o_full[1]))
+                    yield True
+            jb += nblk
+
+    def softmax(t, w):
+        jb = 0
+        for k in range(units):
+            for j in range(nblk):
+                jj = jb + j
+                yield from wait(s_full[t], jj)
+                if sbuf[t][w] != ("S", jj, 0):
+                    raise Fail(f"tile {t} warp {w} reads {sbuf[t][w]}, want S_{jj}")
+                yield True
+                if j > 0 and (j == 0 or rng.random() < p_rescale):
+                    if o_last[t] != (jj - 1, 1):
+                        raise Fail(f"rescale tile {t} at {jj}: O last written by {o_last[t]}")
+                for half in range(2):
+                    sbuf[t][w] = ("P", jj, half + 1)
+                    p_half[2 * t + half].arrive()
+                    yield True
+            jb += nblk
+            yield from wait(o_full[t], k)
+            if o_last[t] != (jb - 1, 1):
+                raise Fail(f"epilogue tile {t} unit {k}: O last written by {o_last[t]}")
+            yield True
+            epi.add((k, t, w))
+            o_empty[t].arrive()
+            yield True
+
+    def pipe_step():
+        if not mma_q:
+            return False
+        op, a = mma_q.pop(0)
+        if op == "commit":
+            a.arrive()
+            return True
+        if op == "S":
+            t, jj, slot, k, j = a
+            if q_tag[0] != k or slot_tag[slot] != ("K", (k, j)):
+                raise Fail(f"S_{t}({jj}) reads Q {q_tag[0]} / slot {slot_tag[slot]}")
+            slot_uses[slot] -= 1
+            for w in range(4):
+                cur = sbuf[t][w]
+                if cur is not None and (cur[0] == "S" or o_last[t] != (cur[1], 1)):
+                    raise Fail(f"S_{t}({jj}) overwrites {cur} before it was consumed")
+                sbuf[t][w] = ("S", jj, 0)
+            s_done[k] = s_done.get(k, 0) + 1
+            return True
+        t, jj, half, slot, k, j = a
+        for w in range(4):
+            cur = sbuf[t][w]
+            if not (cur and cur[0] == "P" and cur[1] == jj and cur[2] >= half + 1):
+                raise Fail(f"PV_{t}({jj}) half {half} reads {cur}")
+        if slot_tag[slot] != ("V", (k, j)):
+            raise Fail(f"PV_{t}({jj}) reads slot {slot_tag[slot]}")
+        if half == 1:
+            slot_uses[slot] -= 1
+        if j == 0 and half == 0 and k > 0 and not all((k - 1, t, w) in epi for w in range(4)):
+            raise Fail(f"unit {k} PV_{t} overwrites O before the epilogue read it")
+        o_last[t] = (jj, half)
+        return True
+
+    def tma_step():
+        if not tma_q:
+            return False
+        kind, tag, slot, bar = tma_q.pop(rng.randrange(len(tma_q)))
+        if kind == "Q":
+            if tag > 0 and s_done.get(tag - 1, 0) != 2 * nblk:
+                raise Fail(f"Q of unit {tag} lands before unit {tag - 1}'s S MMAs ran")
+            q_tag[0] = tag
+        else:
+            if slot_uses[slot] != 0:
+                raise Fail(f"{kind}{tag} overwrites slot {slot} ({slot_tag[slot]}) in use")
+            slot_tag[slot], slot_uses[slot] = (kind, tag), 2
+        bar.arrive()
+        return True
+
+    live = {"prod": producer(), "mma": mma()}
+    for t in range(2):
+        for w in range(4):
+            live[f"sm{t}{w}"] = softmax(t, w)
+    _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q)
+
+
+def _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q):
+    """Runs the roles under a random scheduler with random stalls until all
+    are done; raises Fail on a deadlock."""
+    sleep, idle, steps = {}, 0, 0
+    while live or mma_q or tma_q:
+        steps += 1
+        if steps > 5_000_000:
+            raise Fail("too many steps")
+        ch = rng.choice(list(live) + ["pipe", "tma"])
+        if sleep.get(ch, 0) > steps:
+            continue
+        if rng.random() < 0.01:
+            sleep[ch] = steps + rng.randint(1, 400)
+            continue
+        if ch == "pipe":
+            progressed = pipe_step()
+        elif ch == "tma":
+            progressed = tma_step()
+        else:
+            try:
+                progressed = bool(next(live[ch]))
+            except StopIteration:
+                del live[ch]
+                progressed = True
+        idle = 0 if progressed else idle + 1
+        if idle > 20000:
+            raise Fail(f"deadlock; live={list(live)} mma_q={mma_q[:3]} tma_q={tma_q[:3]}")
+
+
 def _configs_single():
     for seed in range(6):
         for qch, vch, nst in ((8, 4, 6), (6, 3, 8)):
@@ -610,6 +807,21 @@ def _configs_pair():
                 for units in (1, 3):
                     yield seed * 100 + nblk * 10 + units, qch, nstk, nstv, nblk, units, \
                         (0.0, 0.3, 1.0)[seed % 3]
+
+
+def test_fa128_protocol():
+    for seed in range(6):
+        for nst in (4, 8):
+            for nblk in (1, 2, 3, 5):
+                for units in (1, 3):
+                    run_fa128(seed * 100 + nblk * 10 + units, nst, nblk, units,
+                              (0.0, 0.3, 1.0)[seed % 3])
+
+
+def test_model_finds_p_overwrite():
+    with pytest.raises(Fail):
+        for seed in range(6):
+            run_fa128(seed, 4, 3, 2, 0.3, pv_first=False)
 
 
 def test_single_cta_protocol():
