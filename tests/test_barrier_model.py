@@ -1,7 +1,7 @@
-"""CPU: randomised models of the attention kernels' mbarrier protocols —
-fa_fwd_tc_kernel (llm-runner_b200/csrc/fa_tc.cuh) and the two wide-head
-kernels (fa_wide.cuh, checked against these models before their first GPU
-run).
+"""CPU: randomised models of the tensor-core kernels' mbarrier protocols —
+fa_fwd_tc_kernel (llm-runner_b200/csrc/fa_tc.cuh), the two wide-head kernels
+(fa_wide.cuh, checked against these models before their first GPU run) and
+the QKV projection's CTA-pair GEMM (qkv_proj.cuh).
 
 Each model runs the kernel's roles as coroutines under a random scheduler
 with random stalls: the TMA producer(s), the MMA-issuing warp, the softmax
@@ -762,6 +762,108 @@ def run_fa128(seed, NST, nblk, units, p_rescale, pv_first=True):
     _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q)
 
 
+def run_qkv_pair(seed, NST, k_blocks, tiles, p_stall=0.0, wait_acc_empty=True):
+    """qkv_proj_pair_kernel (qkv_proj.cuh): per tile, k_blocks stages through
+    an NST-slot ring (each CTA loads its half; both CTAs' bytes complete on
+    the even CTA's full[st], which the even CTA arms); the even CTA's MMA
+    warp accumulates a tile into TMEM buffer local % 2 and commits empty[st]
+    and acc_full[buf] to both CTAs; 4 epilogue warps per CTA read their rows
+    and arrive on the even CTA's acc_empty[buf] (8 arrivals).
+    wait_acc_empty=False plants a bug: a tile accumulates into a TMEM buffer
+    the epilogues may still be reading."""
+    rng = random.Random(seed)
+    full = [TxBar(f"full{i}", 1) for i in range(NST)]
+    empty = [[Bar(f"empty{i}@{r}", 1) for r in range(2)] for i in range(NST)]
+    acc_full = [[Bar(f"acc_full{b}@{r}", 1) for r in range(2)] for b in range(2)]
+    acc_empty = [Bar(f"acc_empty{b}", 8) for b in range(2)]
+    stage = [[None] * NST for _ in range(2)]       # (tile, kb) held per CTA and slot
+    used = [[True] * NST for _ in range(2)]
+    acc = [None, None]                              # (tile, k blocks accumulated)
+    read = set()
+    tma_q, mma_q = [], []
+
+    def producer(r):
+        it = 0
+        for t in range(tiles):
+            for kb in range(k_blocks):
+                st, rnd = it % NST, it // NST
+                if rnd > 0:
+                    yield from wait(empty[st][r], rnd - 1)
+                if r == 0:
+                    full[st].arrive(expect=2)
+                tma_q.append((r, st, (t, kb), rnd))
+                it += 1
+                yield True
+
+    def mma():
+        it = 0
+        for local in range(tiles):
+            buf = local & 1
+            if local >= 2 and wait_acc_empty:
+                yield from wait(acc_empty[buf], (local >> 1) - 1)
+            for kb in range(k_blocks):
+                st = it % NST
+                yield from wait(full[st], it // NST)
+                mma_q.append(("MMA", (local, kb, st, buf)))
+                mma_q.append(("commit", empty[st][0]))
+                mma_q.append(("commit", empty[st][1]))
+                it += 1
+                yield True
+            mma_q.append(("commit", acc_full[buf][0]))
+            mma_q.append(("commit", acc_full[buf][1]))
+
+    def epilogue(r, w):
+        for local in range(tiles):
+            buf = local & 1
+            yield from wait(acc_full[buf][r], local >> 1)
+            if acc[buf] != (local, k_blocks):
+                raise Fail(f"epilogue of tile {local} reads {acc[buf]}")
+            if rng.random() < p_stall:
+                yield False
+            read.add((local, r, w))
+            acc_empty[buf].arrive()
+            yield True
+
+    def pipe_step():
+        if not mma_q:
+            return False
+        op, a = mma_q.pop(0)
+        if op == "commit":
+            a.arrive()
+            return True
+        local, kb, st, buf = a
+        for r in range(2):
+            if stage[r][st] != (local, kb):
+                raise Fail(f"MMA of tile {local} k {kb} reads stage {stage[r][st]} on CTA {r}")
+            used[r][st] = True
+        if kb == 0:
+            if local >= 2 and not all((local - 2, r, w) in read
+                                      for r in range(2) for w in range(4)):
+                raise Fail(f"tile {local} overwrites accumulator {buf} before it was read")
+            acc[buf] = (local, 1)
+        else:
+            if acc[buf] != (local, kb):
+                raise Fail(f"accumulator {buf} holds {acc[buf]} at tile {local} k {kb}")
+            acc[buf] = (local, kb + 1)
+        return True
+
+    def tma_step():
+        if not tma_q:
+            return False
+        r, st, tag, rnd = tma_q.pop(rng.randrange(len(tma_q)))
+        if not used[r][st]:
+            raise Fail(f"CTA {r} reloads stage {st} with {tag} before its MMA ran")
+        stage[r][st], used[r][st] = tag, False
+        full[st].complete_tx(1, rnd)
+        return True
+
+    live = {"prod0": producer(0), "prod1": producer(1), "mma": mma()}
+    for r in range(2):
+        for w in range(4):
+            live[f"epi{r}{w}"] = epilogue(r, w)
+    _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q)
+
+
 def _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q):
     """Runs the roles under a random scheduler with random stalls until all
     are done; raises Fail on a deadlock."""
@@ -816,6 +918,21 @@ def test_fa128_protocol():
                 for units in (1, 3):
                     run_fa128(seed * 100 + nblk * 10 + units, nst, nblk, units,
                               (0.0, 0.3, 1.0)[seed % 3])
+
+
+def test_qkv_pair_protocol():
+    for seed in range(8):
+        for nst in (4, 6):
+            for k_blocks in (1, 3, 7):
+                for tiles in (1, 3, 5):
+                    run_qkv_pair(seed * 100 + k_blocks * 10 + tiles, nst, k_blocks, tiles,
+                                 (0.0, 0.5)[seed % 2])
+
+
+def test_model_finds_accumulator_overwrite():
+    with pytest.raises(Fail, match="overwrites accumulator"):
+        for seed in range(20):
+            run_qkv_pair(seed, 4, 3, 5, 0.5, wait_acc_empty=False)
 
 
 def test_model_finds_p_overwrite():
