@@ -507,20 +507,33 @@ def cpu_table(args):
                   flush=True)
 
 
+def configs_module():
+    """llmr_attn/configs.py loaded as a standalone module (numpy only)."""
+    import importlib.util
+    path = os.path.join(ROOT, "llm-runner_b200", "llmr_attn", "configs.py")
+    spec = importlib.util.spec_from_file_location("llmr_bench_configs", path)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[spec.name] = mod  # dataclasses resolve the module by name
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def run_reference(args):
     """CPU reference arm: rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     import numpy as np
-    import llmr_attn as L
-    from llmr_attn import configs as C
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    # The configurations' input recipe is pure numpy; it is loaded by path so
+    # that this arm never imports the product package (which maps the CUDA
+    # library), and the RoPE tables come from the oracle's own builder.
+    C = configs_module()
     cores = host_cores()
     O.set_threads(cores)     # torchrun sets OMP_NUM_THREADS=1 per process
     case = C.CASES[args.config]
-    prep = C.prepare(case, L.rope_tables)
+    prep = C.prepare(case, O.rope_tables)
     S, H, D = case.seq_len, case.n_heads, case.head_dim
     split = min(case.split_row, S)
     qb, kb, vb = (np.ascontiguousarray(a[0].reshape(S, H * D)) for a in (prep.q, prep.k, prep.v))

@@ -345,8 +345,8 @@ int llmr_attention_varlen(llmr_ctx *ctx, const llmr_attn_desc *desc,
  *  - The first call on each device looks up the scratch address; make that
  *    first call before any stream capture.
  *  - All calls share the scratch: calls that overlap on the GPU race.
- *  - LLMR_EXACT is rejected (LLMR_EINVAL). The call does not synchronise and
- *    does not report device-side timeouts.
+ *  - LLMR_EXACT is rejected (LLMR_EINVAL). The call does not synchronise;
+ *    a device-side wait that timed out is reported by llmr_noalloc_status.
  * Returns a status code only (there is no context for a message). */
 #define LLMR_NOALLOC_SCRATCH_BYTES ((size_t)64 << 20)
 int llmr_attention_fused_noalloc(const llmr_attn_desc *desc, const void *q,
@@ -354,6 +354,14 @@ int llmr_attention_fused_noalloc(const llmr_attn_desc *desc, const void *q,
                                  const float *q_gain, const float *k_gain,
                                  const float *cos_t, const float *sin_t,
                                  void *o, float *lse, void *stream);
+
+/* Synchronises `stream` (NULL = the default stream) and reports whether any
+ * llmr_attention_fused_noalloc call on the current device since the last
+ * status query had a bounded device-side wait expire: LLMR_ETIMEOUT (the
+ * results of those calls are invalid; the flag is cleared) or LLMR_OK.
+ * Allocates nothing. No counterpart in the reference (its fence waits are
+ * unbounded). */
+int llmr_noalloc_status(void *stream);
 
 /* The prologue of llmr_attention_fused on its own: per-head RMSNorm and RoPE
  * of Q and K, cast of V, written as dense fp16 [3][B][H][S][D] to `qkv_out`

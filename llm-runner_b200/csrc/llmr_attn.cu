@@ -22,6 +22,7 @@
 #include "../../include/llmr_attn.h"
 #include "fa_tc.cuh"
 #include "fa_wide.cuh"
+#include "kattr.cuh"
 #include "kernels_misc.cuh"
 #include "qkv_proj.cuh"
 
@@ -137,13 +138,7 @@ template <int D, int BN, bool BF16>
 int launch_qkv(llmr_ctx *ctx, const void *x, long long x_rs, const void *w, QkvParams &p,
                long long hidden) {
   using C = QkvCfg<D, BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    CUDA_TRY(ctx, cudaFuncSetAttribute(qkv_proj_kernel<D, BN, BF16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::SMEM_BYTES));
-    attr_set = true;
-  }
+  CUDA_TRY(ctx, set_smem_once(qkv_proj_kernel<D, BN, BF16>, C::SMEM_BYTES));
   CUtensorMap mx, mw;
   int rc;
   if ((rc = make_map2d(ctx, &mx, x, hidden, p.M, x_rs, C::BM))) return rc;
@@ -158,13 +153,7 @@ template <bool BF16>
 int launch_out_proj(llmr_ctx *ctx, const CUtensorMap &mx, const CUtensorMap &mw0,
                     const CUtensorMap &mw1, const ProjParams &p) {
   using C = QkvCfg<128, 256>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    CUDA_TRY(ctx, cudaFuncSetAttribute(out_proj_kernel<BF16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kProjSmemBytes));
-    attr_set = true;
-  }
+  CUDA_TRY(ctx, set_smem_once(out_proj_kernel<BF16>, kProjSmemBytes));
   const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
   const int grid = p.tiles < sms ? p.tiles : sms;
   out_proj_kernel<BF16><<<grid, C::THREADS, kProjSmemBytes, ctx->stream>>>(mx, mw0, mw1, p);
@@ -175,13 +164,7 @@ template <int D, bool BF16>
 int launch_qkv_pair(llmr_ctx *ctx, const void *x, long long x_rs, const void *w, QkvParams &p,
                     long long hidden) {
   using C = Qkv2Cfg<D>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    CUDA_TRY(ctx, cudaFuncSetAttribute(qkv_proj_pair_kernel<D, BF16>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::SMEM_BYTES));
-    attr_set = true;
-  }
+  CUDA_TRY(ctx, set_smem_once(qkv_proj_pair_kernel<D, BF16>, C::SMEM_BYTES));
   CUtensorMap mx, mw;
   int rc;
   if ((rc = make_map2d(ctx, &mx, x, hidden, p.M, x_rs, C::BM))) return rc;
@@ -199,20 +182,14 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                  long long o_rs, long long o_bs, float *lse, int merge, int nseq,
                  const int *seq_off) {
   using C = FaCfg<D>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    CUDA_TRY(ctx, cudaFuncSetAttribute(fa_fwd_tc_kernel<D, OutT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::SMEM_BYTES));
-    // setmaxnreg.inc waits until the registers it asks for are free within
-    // the block's launch allocation: never launch a split that cannot fit.
-    cudaFuncAttributes fa;
-    CUDA_TRY(ctx, cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, OutT>));
-    if (fa.numRegs * C::THREADS < C::REG_NEED)
-      return fail(ctx, LLMR_ECUDA, "fa_fwd_tc: %d launch registers per thread are too few "
-                  "for the register split", fa.numRegs);
-    attr_set = true;
-  }
+  CUDA_TRY(ctx, set_smem_once(fa_fwd_tc_kernel<D, OutT>, C::SMEM_BYTES));
+  // setmaxnreg.inc waits until the registers it asks for are free within
+  // the block's launch allocation: never launch a split that cannot fit.
+  int regs = 0;
+  CUDA_TRY(ctx, launch_regs(fa_fwd_tc_kernel<D, OutT>, &regs));
+  if (regs * C::THREADS < C::REG_NEED)
+    return fail(ctx, LLMR_ECUDA, "fa_fwd_tc: %d launch registers per thread are too few "
+                "for the register split", regs);
   FaParams p;
   p.S = S;
   p.S_kv = S_kv;
@@ -356,16 +333,10 @@ int launch_fa_wide(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                    const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
                    long long o_rs, long long o_bs, float *lse) {
   using C = FaWideCfg<D>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (smem_optin(ctx) < C::SMEM_BYTES)
-      return fail(ctx, LLMR_ECUDA, "fa_wide_tc needs %d bytes of shared memory per block",
-                  C::SMEM_BYTES);
-    CUDA_TRY(ctx, cudaFuncSetAttribute(fa_wide_tc_kernel<D, OutT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::SMEM_BYTES));
-    attr_set = true;
-  }
+  if (smem_optin(ctx) < C::SMEM_BYTES)
+    return fail(ctx, LLMR_ECUDA, "fa_wide_tc needs %d bytes of shared memory per block",
+                C::SMEM_BYTES);
+  CUDA_TRY(ctx, set_smem_once(fa_wide_tc_kernel<D, OutT>, C::SMEM_BYTES));
   FaParams p;
   memset(&p, 0, sizeof p);
   p.S = S;
@@ -387,16 +358,10 @@ int launch_fa_wide_pair(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap 
                         const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale,
                         void *o, long long o_rs, long long o_bs, float *lse) {
   using C = FaWide2Cfg<D>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (smem_optin(ctx) < C::SMEM_BYTES)
-      return fail(ctx, LLMR_ECUDA, "fa_wide_pair needs %d bytes of shared memory per block",
-                  C::SMEM_BYTES);
-    CUDA_TRY(ctx, cudaFuncSetAttribute(fa_wide_pair_kernel<D, OutT>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       C::SMEM_BYTES));
-    attr_set = true;
-  }
+  if (smem_optin(ctx) < C::SMEM_BYTES)
+    return fail(ctx, LLMR_ECUDA, "fa_wide_pair needs %d bytes of shared memory per block",
+                C::SMEM_BYTES);
+  CUDA_TRY(ctx, set_smem_once(fa_wide_pair_kernel<D, OutT>, C::SMEM_BYTES));
   FaParams p;
   memset(&p, 0, sizeof p);
   p.S = S;
@@ -480,14 +445,9 @@ template <int D>
 int launch_exact_wide_t(llmr_ctx *ctx, const float *q, const float *k, const float *v,
                         const ExactParams &ep) {
   constexpr int smem = exact_wide_smem(D);
-  static bool attr_set = false;
-  if (!attr_set) {
-    if (smem_optin(ctx) < smem)
-      return fail(ctx, LLMR_ECUDA, "attn_exact_wide needs %d bytes of shared memory", smem);
-    CUDA_TRY(ctx, cudaFuncSetAttribute(attn_exact_wide_kernel<D>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    attr_set = true;
-  }
+  if (smem_optin(ctx) < smem)
+    return fail(ctx, LLMR_ECUDA, "attn_exact_wide needs %d bytes of shared memory", smem);
+  CUDA_TRY(ctx, set_smem_once(attn_exact_wide_kernel<D>, smem));
   constexpr int rows_per_cta = 4 * kExactWideRows;
   dim3 grid((ep.S + rows_per_cta - 1) / rows_per_cta, ep.B * ep.H);
   attn_exact_wide_kernel<D><<<grid, 128, smem, ctx->stream>>>(q, k, v, ep);

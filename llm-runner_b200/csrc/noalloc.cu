@@ -33,12 +33,14 @@
 
 #include "../../include/llmr_attn.h"
 #include "fa_tc.cuh"
+#include "kattr.cuh"
 #include "prologue.cuh"
 
 using namespace llmr;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[LLMR_NOALLOC_SCRATCH_BYTES];
-// Raised by a kernel whose bounded wait expired (set only, never read here).
+// Raised by a kernel of this entry point whose bounded wait expired; read
+// and cleared by llmr_noalloc_status.
 static __device__ int g_noalloc_err;
 
 namespace {
@@ -148,18 +150,13 @@ int attention(cudaStream_t st, int num_sms, const CUtensorMap &mq, const CUtenso
               const CUtensorMap &mv, int B, int H, int S, float scale, void *o, long long o_rs,
               long long o_bs, float *lse, int *err) {
   using C = FaCfg<D>;
-  static bool attr_set = false;  // per-process, like a kernel attribute
-  if (!attr_set) {
-    if (cudaFuncSetAttribute(fa_fwd_tc_kernel<D, OutT>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             C::SMEM_BYTES) != cudaSuccess)
-      return LLMR_ECUDA;
-    cudaFuncAttributes fa;  // the register split must fit (see llmr_attn.cu)
-    if (cudaFuncGetAttributes(&fa, fa_fwd_tc_kernel<D, OutT>) != cudaSuccess ||
-        fa.numRegs * C::THREADS < C::REG_NEED)
-      return LLMR_ECUDA;
-    attr_set = true;
-  }
+  // The shared-memory limit is a per-device attribute: raised once per
+  // device (thread-safe), like the rest of the per-device set-up.
+  if (set_smem_once(fa_fwd_tc_kernel<D, OutT>, C::SMEM_BYTES) != cudaSuccess) return LLMR_ECUDA;
+  int regs = 0;  // the register split must fit the launch allocation
+  if (launch_regs(fa_fwd_tc_kernel<D, OutT>, &regs) != cudaSuccess ||
+      regs * C::THREADS < C::REG_NEED)
+    return LLMR_ECUDA;
   FaParams p;
   p.S = S;
   p.S_kv = S;
@@ -279,4 +276,20 @@ extern "C" int llmr_attention_fused_noalloc(const llmr_attn_desc *d, const void 
                               o_rs, o_bs, lse_out, dev->err);
   return attention_any<64>(st, dev->num_sms, d->out_dtype, mq, mk, mv, B, H, S, d->scale, o,
                            o_rs, o_bs, lse_out, dev->err);
+}
+
+extern "C" int llmr_noalloc_status(void *stream) {
+  DeviceSetup *dev = nullptr;
+  int rc = setup_current_device(&dev);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int h = 0;
+  if (cudaMemcpyAsync(&h, dev->err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return LLMR_ECUDA;
+  if (h == 0) return LLMR_OK;
+  if (cudaMemsetAsync(dev->err, 0, sizeof(int), st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return LLMR_ECUDA;
+  return LLMR_ETIMEOUT;
 }

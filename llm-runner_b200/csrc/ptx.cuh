@@ -456,8 +456,10 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
 // Range reduction: adding 1.5*2^23 rounds x to the nearest integer n in the
 // low mantissa bits (t), so f = x - n lies in [-0.5, 0.5]. 2^f comes from a
 // degree-4 polynomial whose coefficients were fitted for this kernel by a
-// Remez exchange on the relative error over [-0.5, 0.5] (max relative error
-// 3.6e-6, far below the 2^-11 rounding of the fp16 P it feeds). 2^n is then
+// Remez exchange on the relative error over [-0.5, 0.5]. The whole routine,
+// evaluated in float32, has a max relative error of 3.7e-6 against exact 2^x
+// over [-125, 15] (a CPU test restates it from these coefficients and checks
+// the bound), far below the 2^-11 rounding of the fp16 P it feeds. 2^n is then
 // applied by adding n << 23 to the bit pattern: t's bits are
 // 0x4B400000 + n, and shifting them left by 23 leaves exactly n << 23.
 // Callers clamp x >= -125 so the result stays a normal fp32.

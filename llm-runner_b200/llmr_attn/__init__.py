@@ -138,6 +138,7 @@ def _load() -> ctypes.CDLL:
         "llmr_convert_f32": (i32, [vp, vp, vp, ctypes.c_int, ctypes.c_size_t]),
         "llmr_attention_fused_noalloc": (i32, [ctypes.POINTER(AttnDesc), vp, vp, vp, vp, vp,
                                                vp, vp, vp, vp, vp]),
+        "llmr_noalloc_status": (i32, [vp]),
         "llmr_rope_tables": (i32, [vp, u32, u32, vp, f32, vp, vp]),
         "llmr_qkv_project": (i32, [vp, ctypes.POINTER(QkvDesc), vp, vp, vp, vp, vp, vp, vp]),
         "llmr_attention_varlen": (i32, [vp, ctypes.POINTER(AttnDesc), vp, u32, vp, vp, vp, vp,
@@ -406,6 +407,19 @@ def attention_fused_noalloc(q, k, v, o, cfg: AttnConfig, *, batch: int, seq_len:
                                           _ptr(o), _ptr(lse), ctypes.c_void_p(raw or None))
     if rc != OK:
         raise LlmrError(rc, "llmr_attention_fused_noalloc")
+
+
+def noalloc_status(stream=None) -> None:
+    """Synchronises `stream` and raises LlmrError(ETIMEOUT) if a bounded
+    device-side wait of an allocation-free call on the current device expired
+    since the last query (llmr_noalloc_status; the flag is cleared)."""
+    import torch
+    if stream is None:
+        stream = torch.cuda.current_stream()
+    raw = stream.cuda_stream if hasattr(stream, "cuda_stream") else stream
+    rc = lib.llmr_noalloc_status(ctypes.c_void_p(raw or None))
+    if rc != OK:
+        raise LlmrError(rc, "llmr_noalloc_status")
 
 
 def attention_prologue(ctx: Context, q, k, v, qkv_out, cfg: AttnConfig, *, batch: int,

@@ -614,3 +614,36 @@ def test_varlen_rejects(ctx):
         L.attention_varlen(ctx, x, x, x, o, L.AttnConfig(n_heads=2, head_dim=128, scale=0.1,
                                                          split_row=8), (32, 32))
     assert ei.value.status == L.EINVAL
+
+
+def test_fused_two_devices_one_process():
+    """One process driving two GPUs (a context per device, calls alternating
+    between them): kernel attributes are per device, so each device must get
+    its own set-up. Every result is checked against the oracle."""
+    torch = _t()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.runner import to_device
+    prep = C.prepare(C.C3, L.rope_tables, seq_len=384, n_heads=2)
+    want = O.attention_block(prep.q[0], prep.k[0], prep.v[0], 2, 128, C.C3.scale,
+                             eps=C.C3.eps, q_gain=prep.q_gain, k_gain=prep.k_gain,
+                             split_row=min(C.C3.split_row, 384), cos=prep.cos, sin=prep.sin)
+    ctxs, cases = [], []
+    for d in (0, 1):
+        torch.cuda.set_device(d)
+        dc = to_device(prep, device=d, out_dtype="f32")
+        c = L.Context(d)
+        c.reserve(L.workspace_bytes(dc.desc()))
+        ctxs.append(c)
+        cases.append(dc)
+    for _ in range(2):
+        for d in (1, 0):  # device 1 first: a per-process flag would skip its set-up
+            cases[d].o.fill_(float("nan"))
+            cases[d].run(ctxs[d])
+            ctxs[d].sync()
+            check(host(cases[d].o)[0], want, what=f"cuda:{d}")
+    for c in ctxs:
+        c.close()
+    torch.cuda.set_device(0)
