@@ -25,6 +25,7 @@
 #pragma once
 #include <type_traits>
 
+#include "prologue.cuh"
 #include "ptx.cuh"
 
 namespace llmr {
@@ -251,6 +252,9 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
+  // Launched right behind the prologue (programmatic dependent launch), the
+  // set-up above overlaps its tail; its output is read only after this.
+  griddep_wait();
 
   if (warp >= 8) {
     reg_dealloc<C::REG_OTHER>();

@@ -180,7 +180,7 @@ template <int D, typename OutT>
 int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                  const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
                  long long o_rs, long long o_bs, float *lse, int merge, int nseq,
-                 const int *seq_off) {
+                 const int *seq_off, bool pdl) {
   using C = FaCfg<D>;
   CUDA_TRY(ctx, set_smem_once(fa_fwd_tc_kernel<D, OutT>, C::SMEM_BYTES));
   // setmaxnreg.inc waits until the registers it asks for are free within
@@ -205,24 +205,56 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   p.seq_off[0] = 0;
   for (int i = 0; i <= p.nseq && p.nseq > 0; i++) p.seq_off[i] = seq_off[i];
   const dim3 grid = fa_grid<D>(p, B, ctx->num_sms);
-  fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
+  if (!pdl) {
+    fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
+    return after_launch(ctx, "fa_fwd_tc");
+  }
+  // Right behind the prologue on the same stream: programmatic dependent
+  // launch lets this grid's CTAs start (barrier init, TMEM allocation) on SMs
+  // the prologue has left; the kernel waits for the prologue's results.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(C::THREADS);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, fa_fwd_tc_kernel<D, OutT>, mq, mk, mv, p));
   return after_launch(ctx, "fa_fwd_tc");
 }
 
 int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
                      const CUtensorMap &mk, const CUtensorMap &mv, int B, int H, int S, int S_kv,
                      float scale, void *o, long long o_rs, long long o_bs, float *lse,
-                     int merge, int nseq = 0, const int *seq_off = nullptr) {
+                     int merge, int nseq = 0, const int *seq_off = nullptr,
+                     bool pdl = false) {
 #define LLMR_FA_ARGS ctx, mq, mk, mv, B, H, S, S_kv, scale, o, o_rs, o_bs, lse
   if (D == 128) {
-    if (od == LLMR_F32) return launch_fa_tc<128, float>(LLMR_FA_ARGS, merge, nseq, seq_off);
-    if (od == LLMR_F16) return launch_fa_tc<128, __half>(LLMR_FA_ARGS, 0, nseq, seq_off);
-    return launch_fa_tc<128, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off);
+    if (od == LLMR_F32) return launch_fa_tc<128, float>(LLMR_FA_ARGS, merge, nseq, seq_off, pdl);
+    if (od == LLMR_F16) return launch_fa_tc<128, __half>(LLMR_FA_ARGS, 0, nseq, seq_off, pdl);
+    return launch_fa_tc<128, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off, pdl);
   }
-  if (od == LLMR_F32) return launch_fa_tc<64, float>(LLMR_FA_ARGS, merge, nseq, seq_off);
-  if (od == LLMR_F16) return launch_fa_tc<64, __half>(LLMR_FA_ARGS, 0, nseq, seq_off);
-  return launch_fa_tc<64, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off);
+  if (od == LLMR_F32) return launch_fa_tc<64, float>(LLMR_FA_ARGS, merge, nseq, seq_off, pdl);
+  if (od == LLMR_F16) return launch_fa_tc<64, __half>(LLMR_FA_ARGS, 0, nseq, seq_off, pdl);
+  return launch_fa_tc<64, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off, pdl);
 #undef LLMR_FA_ARGS
+}
+
+// LLMR_NO_PDL launches the attention kernel after the prologue without
+// programmatic dependent launch (for comparisons).
+bool pdl_disabled() {
+  static const bool v = getenv("LLMR_NO_PDL") != nullptr;
+  return v;
+}
+
+// LLMR_PROLOGUE_LEGACY selects the one-(tensor, head)-per-CTA prologue
+// (for comparisons).
+bool prologue_legacy() {
+  static const bool v = getenv("LLMR_PROLOGUE_LEGACY") != nullptr;
+  return v;
 }
 
 template <int D, typename InT, typename OutT>
@@ -243,6 +275,17 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
   };
   const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs) && ok(pp.cos_t, nullptr) &&
                    ok(pp.sin_t, nullptr);
+  // The streaming form also reads the gains 16 bytes at a time.
+  if (vec && ok(pp.q_gain, nullptr) && ok(pp.k_gain, nullptr) && !prologue_legacy()) {
+    CUDA_TRY(ctx, set_smem_once(prologue_stream_kernel<D, InT, OutT>, kPsSmemBytes));
+    const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
+    const int hc = prologue_stream_hchunk(pp.B, pp.S, pp.H, sms);
+    const int items = pp.B * ((pp.S + kPsTokens - 1) / kPsTokens) * ((pp.H + hc - 1) / hc);
+    const int grid = items < 2 * sms ? items : 2 * sms;
+    prologue_stream_kernel<D, InT, OutT><<<grid, 32 * kPsWarps, kPsSmemBytes, ctx->stream>>>(
+        vq, vk, vv, out, pp, hc, items);
+    return after_launch(ctx, "prologue_stream");
+  }
   if (vec)
     prologue_kernel<D, InT, OutT, true><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   else
@@ -924,7 +967,8 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
                             d->scale, o, o_rs, o_bs, lse_out);
   else
     rc = launch_fa_tc_any(ctx, D, d->out_dtype, mq, mk, mv, B, H, S, S_kv, d->scale, o, o_rs,
-                          o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0, nseq, seq_off);
+                          o_bs, lse_out, (d->flags & LLMR_MERGE) ? 1 : 0, nseq, seq_off,
+                          /*pdl=*/!direct && !ctx->prof_on && !pdl_disabled());
   mark(2);
   ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
   return rc;
