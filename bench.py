@@ -38,6 +38,8 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default="flux_1024")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-strong", action="store_true",
+                    help="with N > 1 GPUs: skip the Qwen-Edit strong-scaling block")
     ap.add_argument("--profile-run", action="store_true",
                     help="only W + K fused calls, nothing else (for ncu captures)")
     ap.add_argument("--mode", choices=["batch", "headsplit", "ring"], default="batch",
@@ -598,6 +600,165 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def f64_rows(q, k, v, qg, kg, cos, sin, case, rows, heads):
+    """fp64 restatement of the fused op for query rows `rows` (a slice) and
+    heads `heads` (a range), on the GPU: per-head RMSNorm with the txt/img
+    gain set of each row, the interleaved RoPE rotation, Q / K / V rounded to
+    fp16 (the reference's load rounding), exact softmax. q/k/v: [1, S, H, D]
+    device tensors; returns [len(rows), len(heads) * D] float64."""
+    import torch
+    S, D = q.shape[1], q.shape[3]
+    split = min(case.split_row, S)
+
+    def prep(x, g, r0, r1, h, rope):
+        x = x[0, r0:r1, h].double()
+        if g is not None:
+            gs = g.double().reshape(-1, D)
+            sel = torch.zeros(r1 - r0, dtype=torch.long, device=x.device)
+            if gs.shape[0] > 1 and split > 0:
+                sel[torch.arange(r0, r1, device=x.device) >= split] = 1
+            x = x * torch.rsqrt((x * x).mean(-1, keepdim=True) + case.eps) * gs[sel]
+        if rope:
+            c, s_ = cos[r0:r1].double(), sin[r0:r1].double()
+            y = torch.empty_like(x)
+            y[:, 0::2] = x[:, 0::2] * c - x[:, 1::2] * s_
+            y[:, 1::2] = x[:, 0::2] * s_ + x[:, 1::2] * c
+            x = y
+        return x.half().double()
+
+    out = []
+    for h in heads:
+        qn = prep(q, qg, rows.start, rows.stop, h, cos is not None)
+        kn = prep(k, kg, 0, S, h, cos is not None)
+        vn = prep(v, None, 0, S, h, False)
+        out.append(torch.softmax((qn @ kn.T) * case.scale, dim=-1) @ vn)
+    return torch.cat(out, dim=1)
+
+
+def strong_scaling_block(args, world, rank, local):
+    """The north star's multi-GPU target, measured inside the same torchrun
+    launch as the weak-scaling line: Qwen-Image-Edit 2048^2 (B1 H24 S33792
+    D128 bf16, QK-RMSNorm + 3-axis RoPE) as ONE attention spread over all
+    ranks (strong scaling), as (a) a head split (H/N heads per GPU, no
+    collective) and (b) the sequence-sharded ring with both K/V transports
+    (copy-engine pulls; NCCL P2P with 0 / 8 / 16 SMs left free for NCCL's
+    kernels). T1 is the same call on rank 0's GPU alone, timed here.
+    Every time is the max over ranks of CUDA-event time; each mode's
+    assembled output is checked on row windows against an fp64 restatement
+    (max / mean error over all ranks)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    import llmr_attn as L
+    from llmr_attn import configs as C
+    from llmr_attn.dist import RingAttention, RingOps, head_split_attention, partition_units
+    from llmr_attn.runner import attn_config
+
+    case = C.CASES["qwen_edit_2048"]
+    S, H, D = case.seq_len, case.n_heads, case.head_dim
+    dev = torch.device(f"cuda:{local}")
+    g = torch.Generator(device=dev).manual_seed(1000 + case.seed)  # identical on every rank
+    q, k, v = (torch.randn((1, S, H, D), device=dev, generator=g).to(torch.bfloat16)
+               for _ in range(3))
+    rng = np.random.default_rng(case.seed)
+    qg = torch.from_numpy(rng.uniform(0.8, 1.2, (2, D)).astype(np.float32)).to(dev)
+    kg = torch.from_numpy(rng.uniform(0.8, 1.2, (2, D)).astype(np.float32)).to(dev)
+    cos, sin = (torch.from_numpy(t).to(dev) for t in
+                L.rope_tables(C.case_ids(case), case.rope[0], case.rope[1]))
+    cfg = attn_config(case, S)
+    steps = max(3, min(args.steps, 10))
+    warm = 2
+    stream = torch.cuda.Stream(device=dev)
+
+    def timed(step_fn, ctx, active=True):
+        with torch.cuda.stream(stream):
+            if active:
+                for _ in range(warm):
+                    step_fn()
+            ctx.sync()
+            dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            if active:
+                for _ in range(steps):
+                    step_fn()
+            b.record(stream)
+            torch.cuda.synchronize()
+            ctx.sync()
+        t = torch.tensor([a.elapsed_time(b) / steps if active else 0.0], dtype=torch.float64,
+                         device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def check(err_max, err_sum, n):
+        t = torch.tensor([err_max], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        u = torch.tensor([err_sum, float(n)], dtype=torch.float64, device=dev)
+        dist.all_reduce(u)
+        return {"max_abs_err": float(t.item()), "mean_abs_err": float(u[0] / max(u[1], 1.0))}
+
+    res = {"workload": f"{case.name}: B1 H{H} S{S} D{D} bf16, QK-RMSNorm + RoPE, one "
+                       f"attention over {world} GPUs", "steps": steps, "warmup": warm,
+           "flop_per_call": case.flops}
+    with torch.cuda.stream(stream):
+        ctx = L.Context(local, stream=stream)
+    # T1: the whole call on one GPU (rank 0), the others idle.
+    o_full = torch.empty((1, S, H * D), dtype=torch.bfloat16, device=dev)
+    ctx.reserve(3 * S * H * D * 2)
+    t1 = timed(lambda: L.attention_fused(ctx, q, k, v, o_full, cfg, batch=1, seq_len=S,
+                                         q_gain=qg, k_gain=kg, cos=cos, sin=sin),
+               ctx, active=rank == 0)
+    res["t1_ms"] = t1
+    windows = [(1008, 1072), (S - 32, S)]
+
+    # (a) head split: H / world heads per GPU, no collective.
+    runs = partition_units(1, H, world, rank)
+    hs_ms = timed(lambda: head_split_attention(ctx, q, k, v, o_full, cfg, batch=1, seq_len=S,
+                                               rank=rank, world=world, q_gain=qg, k_gain=kg,
+                                               cos=cos, sin=sin), ctx)
+    emax, esum, n = 0.0, 0.0, 0
+    for _, h0, h1 in runs:
+        for r0, r1 in windows:
+            want = f64_rows(q, k, v, qg, kg, cos, sin, case, range(r0, r1), range(h0, h1))
+            err = (o_full[0, r0:r1, h0 * D:h1 * D].double() - want).abs()
+            emax, esum, n = max(emax, err.max().item()), esum + err.sum().item(), n + err.numel()
+    res["headsplit"] = {"ms": hs_ms, "efficiency": t1 / (world * hs_ms),
+                        "heads_per_gpu": f"{H // world}" if H % world == 0 else "uneven",
+                        **check(emax, esum, n)}
+
+    # (b) sequence ring: rank r holds tokens [r*S/N, (r+1)*S/N).
+    s_loc = S // world
+    sl = slice(rank * s_loc, (rank + 1) * s_loc)
+    qs, ks, vs = (x[:, sl].contiguous() for x in (q, k, v))
+    o_loc = torch.empty((1, s_loc, H * D), dtype=torch.bfloat16, device=dev)
+    for transport, reserve in (("copy", 0), ("nccl", 0), ("nccl", 8), ("nccl", 16)):
+        with torch.cuda.stream(stream):
+            rctx = L.Context(local, stream=stream)
+            if reserve:
+                rctx.set_sm_budget(torch.cuda.get_device_properties(dev).multi_processor_count
+                                   - reserve)
+            ring = RingAttention(RingOps(rctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
+                                 dev, transport=transport)
+        ms = timed(lambda: ring.forward(qs, ks, vs, o_loc, qg, kg, cos, sin), rctx)
+        w0 = rank * s_loc
+        want = f64_rows(q, k, v, qg, kg, cos, sin, case, range(w0, w0 + 64), range(H))
+        err = (o_loc[0, :64].double() - want).abs()
+        key = "ring_copy" if transport == "copy" else f"ring_nccl_free_sms_{reserve}"
+        res[key] = {"ms": ms, "efficiency": t1 / (world * ms),
+                    **check(err.max().item(), err.sum().item(), err.numel())}
+        torch.cuda.synchronize()
+        dist.barrier()
+        ring.close()
+        rctx.close()
+    ctx.close()
+    tflops = {k_: case.flops / (v_["ms"] / 1e3) / 1e12 for k_, v_ in res.items()
+              if isinstance(v_, dict) and "ms" in v_}
+    res["tflops_whole_job"] = tflops
+    return res
+
+
 def run_strong(args):
     """One attention of the configuration spread over all ranks (strong
     scaling): `headsplit` gives each rank a contiguous share of the (b, h)
@@ -937,6 +1098,8 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if world > 1 and not args.no_strong:
+        line["strong_scaling"] = strong_scaling_block(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tf, rows, dt = cpu_sample(case, prep)
         line["cpu_baseline"] = {

@@ -81,6 +81,11 @@ int llmr_ctx_destroy(llmr_ctx *ctx);
 /* Grow the workspace to at least `bytes` (synchronous; not for the hot loop). */
 int llmr_ctx_reserve(llmr_ctx *ctx, size_t bytes);
 int llmr_set_stream(llmr_ctx *ctx, void *stream);
+/* Limit the persistent kernels of this context to `sms` SMs (0 = all SMs of
+ * the device), leaving the rest to work that runs beside them, e.g. the
+ * NCCL send/receive kernels of the sequence-sharded ring. No reference
+ * counterpart (the reference is single-GPU). */
+int llmr_ctx_set_sm_budget(llmr_ctx *ctx, int sms);
 void *llmr_get_stream(llmr_ctx *ctx);
 const char *llmr_last_error(llmr_ctx *ctx);
 /* Wait for all work on the context stream; reports device-side timeouts.

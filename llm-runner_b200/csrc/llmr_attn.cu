@@ -250,13 +250,6 @@ bool pdl_disabled() {
   return v;
 }
 
-// LLMR_PROLOGUE_LEGACY selects the one-(tensor, head)-per-CTA prologue
-// (for comparisons).
-bool prologue_legacy() {
-  static const bool v = getenv("LLMR_PROLOGUE_LEGACY") != nullptr;
-  return v;
-}
-
 template <int D, typename InT, typename OutT>
 int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v,
                       const long long *qs, const long long *ks, const long long *vs,
@@ -275,17 +268,6 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
   };
   const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs) && ok(pp.cos_t, nullptr) &&
                    ok(pp.sin_t, nullptr);
-  // The streaming form also reads the gains 16 bytes at a time.
-  if (vec && ok(pp.q_gain, nullptr) && ok(pp.k_gain, nullptr) && !prologue_legacy()) {
-    CUDA_TRY(ctx, set_smem_once(prologue_stream_kernel<D, InT, OutT>, kPsSmemBytes));
-    const int sms = ctx->num_sms > 0 ? ctx->num_sms : 148;
-    const int hc = prologue_stream_hchunk(pp.B, pp.S, pp.H, sms);
-    const int items = pp.B * ((pp.S + kPsTokens - 1) / kPsTokens) * ((pp.H + hc - 1) / hc);
-    const int grid = items < 2 * sms ? items : 2 * sms;
-    prologue_stream_kernel<D, InT, OutT><<<grid, 32 * kPsWarps, kPsSmemBytes, ctx->stream>>>(
-        vq, vk, vv, out, pp, hc, items);
-    return after_launch(ctx, "prologue_stream");
-  }
   if (vec)
     prologue_kernel<D, InT, OutT, true><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   else
@@ -573,6 +555,16 @@ int llmr_set_stream(llmr_ctx *ctx, void *stream) {
     ctx->own_stream = false;
   }
   ctx->stream = static_cast<cudaStream_t>(stream);
+  return LLMR_OK;
+}
+
+int llmr_ctx_set_sm_budget(llmr_ctx *ctx, int sms) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+  int all = 0;
+  CUDA_TRY(ctx, cudaDeviceGetAttribute(&all, cudaDevAttrMultiProcessorCount, ctx->device));
+  if (sms < 0 || sms > all) return fail(ctx, LLMR_EINVAL, "sm budget %d outside [0, %d]", sms, all);
+  ctx->num_sms = sms == 0 ? all : sms;
   return LLMR_OK;
 }
 

@@ -110,6 +110,7 @@ def _load() -> ctypes.CDLL:
         "llmr_ctx_destroy": (i32, [vp]),
         "llmr_ctx_reserve": (i32, [vp, ctypes.c_size_t]),
         "llmr_set_stream": (i32, [vp, vp]),
+        "llmr_ctx_set_sm_budget": (i32, [vp, i32]),
         "llmr_get_stream": (vp, [vp]),
         "llmr_last_error": (ctypes.c_char_p, [vp]),
         "llmr_sync": (i32, [vp]),
@@ -205,6 +206,10 @@ class Context:
 
     def reserve(self, nbytes: int) -> None:
         self.check(lib.llmr_ctx_reserve(self.handle, nbytes))
+
+    def set_sm_budget(self, sms: int) -> None:
+        """Persistent kernels of this context use at most `sms` SMs (0 = all)."""
+        self.check(lib.llmr_ctx_set_sm_budget(self.handle, sms))
 
     def sync(self) -> None:
         self.check(lib.llmr_sync(self.handle))
