@@ -190,7 +190,11 @@ int llmr_mrope(llmr_ctx *ctx, float *data, const float *cos_t,
  * dependencies/depth_anything.c3l/depth_anything.c3:335-337). q,k,v,o:
  * [n_heads, seq_len, head_dim] fp32, exact softmax. `scores` is accepted for
  * signature compatibility and ignored (may be NULL): no S x S buffer is
- * materialised. head_dim 64 or 128. */
+ * materialised. head_dim 64 or 128. head_dim 64 runs on the tensor cores
+ * (three TF32 products per fp32 product, fp32 accumulation) when the
+ * context workspace holds 3*n_heads*seq_len*64*4 bytes (llmr_ctx_reserve)
+ * for the operands' TF32 residuals; otherwise, and for head_dim 128, on an
+ * fp32 FMA kernel. Both stay within 1e-5 of the reference's arithmetic. */
 int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k,
                            const float *v, float *scores, float *o,
                            uint32_t head_dim, uint32_t n_heads,

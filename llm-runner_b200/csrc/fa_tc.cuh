@@ -54,6 +54,79 @@ struct FaParams {
   int *err;              // device error word (nonzero on timeout)
 };
 
+// The prologue fused into the attention kernel (the fused op's default for
+// 16-bit inputs): the kernel itself writes the fp16 Q', K', V' its TMA maps
+// read. Work is cut into pieces of 32 token rows of one (tensor, b, h).
+//  * Start-up: every warp of every CTA writes the K'/V' pieces of the (b, h)
+//    pairs that the first round of units touches (spread round-robin over
+//    all warps of the grid), and the CTA's own warps write the Q' of its
+//    first unit.
+//  * Background: warps 10-11 (otherwise idle) write the Q' of the CTA's next
+//    unit, then the K'/V' pieces of the remaining (b, h) pairs in order, then
+//    the Q' of the later units, while the other warps run attention.
+//  * sync[1 + b*H + h] counts the K'/V' pieces of (b, h) written (released
+//    after the pieces' stores); a unit's K/V loads wait until it reaches
+//    2 * nrb. Q' of a later unit is handed to the producer through a
+//    per-warp counter in shared memory. The last CTA to finish resets sync[] to zero, so the
+//    buffer is ready for the next launch without a memset.
+// All CTAs must be resident together (they wait for pieces written by
+// others): the kernel is launched cooperatively with at most one CTA per SM.
+struct FusedPro {
+  const void *q, *k, *v;          // raw inputs (fp16 / bf16)
+  long long qs[3], ks[3], vs[3];  // {batch, row, head} strides in elements
+  __half *ws;                     // Q', K', V' fp16 [3][B][H][S][D]
+  int *sync;                      // [0] CTAs finished, [1 + bh] pieces ready
+  ProParams pp;
+  int nrb;                        // 32-row pieces per (b, h) and tensor
+  int startup_bh;                 // (b, h) pairs written in the start-up phase
+};
+
+// Bounded wait until the global counter reaches `target` (acquire).
+__device__ __forceinline__ bool counter_wait(const int *ctr, int target,
+                                             volatile int *abort_flag) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(ctr) : "memory");
+    if (v >= target) return true;
+    if ((++n & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > LLMR_WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
+
+// Bounded wait until a counter in shared memory, written by another warp of
+// the CTA after a __threadfence, reaches `target`.
+__device__ __forceinline__ bool smem_counter_wait(volatile int *ctr, int target,
+                                                  volatile int *abort_flag) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (*ctr < target) {
+    if ((++n & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > LLMR_WAIT_LIMIT_NS) {
+        *abort_flag = 1;
+        return false;
+      }
+    }
+    __nanosleep(32);
+  }
+  __threadfence();
+  return true;
+}
+
+// Orders this thread's generic-proxy global writes before later async-proxy
+// (TMA) reads of them, by any thread that synchronises with this one.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 template <int D>
 struct FaCfg {
   static constexpr int BM = 128;                 // query rows per tile
@@ -68,13 +141,18 @@ struct FaCfg {
   // barriers: q_full, q_empty, kv_full[NST], kv_empty[NST], s_full[2],
   // p_half[2][2] (P of keys 0-63 / 64-127 of tile t written), o_full[2],
   // o_empty[2], drain; then tmem base word and abort flag
-  static constexpr int NBAR = 2 + 2 * NST + 2 + 4 + 2 + 2 + 1;
-  static constexpr int SMEM_BYTES = BAR_OFF + NBAR * 8 + 16 + 1024;  // +align slack
+  static constexpr int NBAR = 2 + 2 * NST + 2 + 4 + 2 + 2 + 1 + 1;  // + q_done[2]
+  // Fused prologue: a cp.async prefetch ring per background warp in the
+  // shared memory left over (the non-fused kernel leaves it unused).
+  static constexpr int BG_OFF = (BAR_OFF + NBAR * 8 + 16 + 127) / 128 * 128;
+  static constexpr int BG_RING = 12 * 1024;  // bytes per background warp
+  static constexpr int SMEM_BYTES = BG_OFF + 2 * BG_RING + 1024;  // +align slack
+  static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static constexpr int THREADS = 384;
   // Register split (setmaxnreg): the two softmax warpgroups hold a whole
   // 128-score row per thread; the producer / MMA warpgroup needs few.
   static constexpr int REG_SOFTMAX = 200;
-  static constexpr int REG_OTHER = 80;
+  static constexpr int REG_OTHER = 104;
   static constexpr int REG_LAUNCH = 168;  // 65536 / 384, rounded down to 8
   static constexpr int REG_NEED = 2 * 128 * REG_SOFTMAX + 128 * REG_OTHER;
   static_assert(REG_NEED <= THREADS * REG_LAUNCH, "register split exceeds the launch allocation");
@@ -159,13 +237,17 @@ __device__ __forceinline__ void store_row_chunk<__nv_bfloat16>(
   }
 }
 
-template <int D, typename OutT>
+// InT = void: Q', K', V' are already in the maps' memory. InT = __half or
+// __nv_bfloat16: the kernel writes them from the raw inputs (FusedPro).
+template <int D, typename OutT, typename InT = void>
 __global__ void __launch_bounds__(384, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
-                     const FaParams p) {
+                     const FaParams p, const __grid_constant__ FusedPro fp) {
   using C = FaCfg<D>;
+  constexpr bool FUSED = !std::is_void<InT>::value;
+  using In = typename std::conditional<FUSED, InT, __half>::type;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment: SW128 atoms must start on 1024-byte boundaries so
   // that the descriptors' base offset is 0.
@@ -184,7 +266,11 @@ __global__ void __launch_bounds__(384, 1)
   uint64_t *o_full = p_half + 4;  // [t]
   uint64_t *o_empty = o_full + 2; // [t]
   uint64_t *drain = o_empty + 2;
-  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  // Fused prologue: units whose Q' each background warp has written (a
+  // warp may run several units ahead of the producer, so counters rather
+  // than an mbarrier's phases).
+  volatile int *q_done = reinterpret_cast<volatile int *>(drain + 1);
+  uint32_t *tmem_base_slot = reinterpret_cast<uint32_t *>(drain + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_base_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -241,6 +327,7 @@ __global__ void __launch_bounds__(384, 1)
       mbar_init(&o_empty[t], 4);
     }
     mbar_init(drain, 1);
+    q_done[0] = q_done[1] = 0;
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -255,6 +342,44 @@ __global__ void __launch_bounds__(384, 1)
   // Launched right behind the prologue (programmatic dependent launch), the
   // set-up above overlaps its tail; its output is read only after this.
   griddep_wait();
+
+  const View<In> vq{static_cast<const In *>(fp.q), fp.qs[0], fp.qs[1], fp.qs[2]};
+  const View<In> vk{static_cast<const In *>(fp.k), fp.ks[0], fp.ks[1], fp.ks[2]};
+  const View<In> vv{static_cast<const In *>(fp.v), fp.vs[0], fp.vs[1], fp.vs[2]};
+  // K'/V' piece i (ordered by (b, h)): tensor 1 + r / nrb, rows 32 * (r % nrb).
+  auto kv_piece = [&](int i) {
+    const int per = 2 * fp.nrb;
+    const int bh = i / per, r = i - bh * per;
+    const int t = 1 + r / fp.nrb, rb = r - (t - 1) * fp.nrb;
+    return make_int4(bh, t, rb, 0);
+  };
+  // Publishes a finished K'/V' piece of (b, h): the pieces' stores, made
+  // visible to the async proxy and at GPU scope, then the counter.
+  auto publish = [&](int bh) {
+    fence_proxy_async_global();
+    __threadfence();
+    __syncwarp();
+    if (lane == 0) atomicAdd(fp.sync + 1 + bh, 1);
+  };
+  if constexpr (FUSED) {
+    // ------------------------------------------------ fused prologue, start-up
+    const int G = gridDim.x;
+    const int nstart = fp.startup_bh * 2 * fp.nrb;
+    for (int i = warp * G + blockIdx.x; i < nstart; i += (C::THREADS / 32) * G) {
+      const int4 pc = kv_piece(i);
+      const int b = pc.x / p.H, h = pc.x - b * p.H;
+      pro_piece<D, In, 4>(vq, vk, vv, fp.ws, fp.pp, pc.y, b, h, pc.z * 32, lane);
+      publish(pc.x);
+    }
+    // Q' of this CTA's first unit: its 8 pieces on warps 0-7.
+    if ((int)blockIdx.x < p.units && warp < 8) {
+      const Unit un = decode(blockIdx.x);
+      const int s0 = un.q0 + warp * 32;
+      if (s0 < un.sq) pro_piece<D, In, 4>(vq, vk, vv, fp.ws, fp.pp, 0, un.b, un.h, s0, lane);
+      fence_proxy_async_global();
+    }
+    __syncthreads();
+  }
 
   if (warp >= 8) {
     reg_dealloc<C::REG_OTHER>();
@@ -276,6 +401,20 @@ __global__ void __launch_bounds__(384, 1)
           if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, abort_flag)) {
             ok = false;
             break;
+          }
+          if constexpr (FUSED) {
+            // Q' of a later unit comes from the background warps; K'/V' of
+            // this (b, h) from pieces written all over the grid.
+            if (k > 0 && !(smem_counter_wait(&q_done[0], k, abort_flag) &&
+                           smem_counter_wait(&q_done[1], k, abort_flag))) {
+              ok = false;
+              break;
+            }
+            if (!counter_wait(fp.sync + 1 + b * p.H + h, 2 * fp.nrb, abort_flag)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
           }
           mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
           for (int t = 0; t < 2; t++)
@@ -401,6 +540,109 @@ __global__ void __launch_bounds__(384, 1)
       // released at the end of the kernel.
       if (elect_one()) mma_commit(drain);
       mbar_wait_raw(drain, 0, 100000000ull);
+    } else if constexpr (FUSED) {
+      // ------------------------------------------- fused prologue, background
+      // The warp's pieces, in order: its 4 pieces of Q' of unit 1 of this
+      // CTA, its share of the remaining K'/V' pieces (ordered by (b, h), so
+      // the pairs the next rounds need come first), its 4 pieces of Q' of
+      // each later unit. Every lane prefetches its own 16-byte parts of the
+      // next steps (4 rows each) into the warp's shared-memory ring and reads
+      // back only what it copied itself.
+      constexpr int E = D / kProLanesPerRow;
+      constexpr int VIN = 16 / sizeof(In);
+      constexpr int CH = E / VIN;
+      constexpr int STEP = 32 * CH * 16;  // bytes of one step (4 rows)
+      constexpr int NSTG = C::BG_RING / STEP > 16 ? 16 : C::BG_RING / STEP;
+      const int G = gridDim.x, wb = warp - 10;
+      const int sub = lane & (kProLanesPerRow - 1), r = lane / kProLanesPerRow;
+      uint8_t *ring_p = smem + C::BG_OFF + wb * C::BG_RING;
+      const uint32_t ring = smem_u32(ring_p);
+      const int my_units = ((int)blockIdx.x < p.units) ? (p.units - (int)blockIdx.x + G - 1) / G : 0;
+      const int nq1 = my_units > 1 ? 4 : 0;
+      const int pairs = p.units > 0 ? (p.units - 1) / p.nqt + 1 : 0;
+      const int kv_all = pairs * 2 * fp.nrb;
+      const int kv0 = fp.startup_bh * 2 * fp.nrb + wb * G + (int)blockIdx.x;
+      const int nkv = kv0 < kv_all ? (kv_all - kv0 + 2 * G - 1) / (2 * G) : 0;
+      const int nqk = my_units > 2 ? 4 * (my_units - 2) : 0;
+      const int nsteps = 8 * (nq1 + nkv + nqk);
+      // Piece pi -> (t, b, h, first row, unit k or -1 for K'/V', index j).
+      struct Pc {
+        int t, b, h, s0, k, j;  // j: the piece's index among the warp's 4 of unit k
+      };
+      auto piece = [&](int pi) {
+        Pc c;
+        int k = -1, j = 0;
+        if (pi < nq1) {
+          k = 1;
+          j = pi;
+        } else if (pi >= nq1 + nkv) {
+          const int rest = pi - nq1 - nkv;
+          k = 2 + rest / 4;
+          j = rest - (rest / 4) * 4;
+        }
+        if (k >= 0) {
+          const Unit un = decode(blockIdx.x + k * G);
+          c.t = 0;
+          c.b = un.b;
+          c.h = un.h;
+          c.s0 = un.q0 + (wb * 4 + j) * 32;
+        } else {
+          const int4 kp = kv_piece(kv0 + (pi - nq1) * 2 * G);
+          c.b = kp.x / p.H;
+          c.h = kp.x - c.b * p.H;
+          c.t = kp.y;
+          c.s0 = kp.z * 32;
+        }
+        c.k = k;
+        c.j = j;
+        return c;
+      };
+      auto issue = [&](int g) {
+        const Pc c = piece(g >> 3);
+        const int s = c.s0 + (g & 7) * kProRowsPerWarpStep + r;
+        const ViewSel<In> v(vq, vk, vv, c.t);
+        const bool in = s < p.S;
+        const In *src = v.base + (long long)c.b * v.bs + (long long)(in ? s : 0) * v.rs +
+                        (long long)c.h * v.hs + sub * E;
+        const uint32_t dst = ring + (uint32_t)((g % NSTG) * STEP) + (uint32_t)lane * 16u;
+#pragma unroll
+        for (int cc = 0; cc < CH; cc++) cp_async16(dst + cc * 512u, src + cc * VIN, in ? 16u : 0u);
+      };
+#pragma unroll 1
+      for (int g = 0; g < NSTG - 1; g++) {
+        if (g < nsteps) issue(g);
+        cp_async_commit();
+      }
+#pragma unroll 1
+      for (int g = 0; g < nsteps; g++) {
+        if ((g & 7) == 0 && *abort_flag) break;
+        if (g + NSTG - 1 < nsteps) issue(g + NSTG - 1);
+        cp_async_commit();
+        cp_async_wait<NSTG - 1>();  // this lane's parts of step g have landed
+        const Pc c = piece(g >> 3);
+        const int s = c.s0 + (g & 7) * kProRowsPerWarpStep + r;
+        const bool in = s < p.S;
+        float x[E];
+        const uint8_t *part = ring_p + (g % NSTG) * STEP + lane * 16;
+#pragma unroll
+        for (int cc = 0; cc < CH; cc++) {
+          const Pack<In, VIN> pk = *reinterpret_cast<const Pack<In, VIN> *>(part + cc * 512);
+#pragma unroll
+          for (int e = 0; e < VIN; e++) x[cc * VIN + e] = in ? to_f32<In>(pk.v[e]) : 0.0f;
+        }
+        pro_row_finish<D>(x, fp.pp, c.t, s, sub, pro_dst<D>(fp.ws, fp.pp, c.t, c.b, c.h, in ? s : 0, sub));
+        if ((g & 7) == 7) {  // piece complete
+          if (c.k < 0) {
+            publish(c.b * p.H + c.h);
+          } else if (c.j == 3) {  // the warp's last Q' piece of unit k
+            fence_proxy_async_global();
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) q_done[wb] = c.k;
+          }
+        }
+      }
+      cp_async_wait<0>();
     }
   } else {
     reg_alloc<C::REG_SOFTMAX>();
@@ -576,6 +818,25 @@ __global__ void __launch_bounds__(384, 1)
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
+  if constexpr (FUSED) {
+    // Every wait of this CTA on the piece counters is over. The last CTA to
+    // get here clears the counters for the next launch.
+    __shared__ int last_cta;
+    if (threadIdx.x == 0) {
+      __threadfence();
+      last_cta = atomicAdd(fp.sync, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (last_cta) {
+      const int pairs = p.units > 0 ? (p.units - 1) / p.nqt + 1 : 0;
+      for (int i = threadIdx.x; i < pairs; i += blockDim.x) fp.sync[1 + i] = 0;
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        fp.sync[0] = 0;
+        __threadfence();
+      }
+    }
+  }
 }
 
 }  // namespace llmr

@@ -20,6 +20,7 @@
 #include <string>
 
 #include "../../include/llmr_attn.h"
+#include "exact_tc.cuh"
 #include "fa_tc.cuh"
 #include "fa_wide.cuh"
 #include "kattr.cuh"
@@ -28,6 +29,8 @@
 
 using namespace llmr;
 
+constexpr size_t kSyncInts = 1 + 65536;
+
 struct llmr_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -35,6 +38,7 @@ struct llmr_ctx {
   void *ws = nullptr;
   size_t ws_bytes = 0;
   int *d_err = nullptr;
+  int *d_sync = nullptr;  // fused-prologue piece counters (self-resetting)
   uint64_t launches = 0;
   int num_sms = 0;
   bool prof_on = false;
@@ -134,6 +138,27 @@ int make_map2d(llmr_ctx *ctx, CUtensorMap *map, const void *base, long long inne
   return LLMR_OK;
 }
 
+// 4-D fp32 tensor map over (d, s, h, b) with a 32 x 128 x 1 x 1 box and
+// 128-byte swizzle (one SW128 K-major or MN-major tf32 operand chunk).
+int make_map_f32(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S, int H, int B,
+                 long long rs, long long hs, long long bs) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((rs * 4) & 15) || ((hs * 4) & 15) ||
+      ((bs * 4) & 15))
+    return fail(ctx, LLMR_EINVAL, "TMA operand base/strides must be 16-byte aligned");
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t strides[3] = {(cuuint64_t)rs * 4, (cuuint64_t)hs * 4, (cuuint64_t)bs * 4};
+  cuuint32_t box[4] = {32, 128, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(base), dims,
+                   strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return LLMR_OK;
+}
+
 template <int D, int BN, bool BF16>
 int launch_qkv(llmr_ctx *ctx, const void *x, long long x_rs, const void *w, QkvParams &p,
                long long hidden) {
@@ -176,17 +201,20 @@ int launch_qkv_pair(llmr_ctx *ctx, const void *x, long long x_rs, const void *w,
   return after_launch(ctx, "qkv_proj_pair");
 }
 
-template <int D, typename OutT>
+// fused != nullptr: the prologue runs inside the attention kernel (InT is
+// the raw input type); the launch is cooperative (all CTAs resident).
+template <int D, typename OutT, typename InT = void>
 int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
                  const CUtensorMap &mv, int B, int H, int S, int S_kv, float scale, void *o,
                  long long o_rs, long long o_bs, float *lse, int merge, int nseq,
-                 const int *seq_off, bool pdl) {
+                 const int *seq_off, bool pdl, const FusedPro *fused = nullptr) {
   using C = FaCfg<D>;
-  CUDA_TRY(ctx, set_smem_once(fa_fwd_tc_kernel<D, OutT>, C::SMEM_BYTES));
+  auto kern = fa_fwd_tc_kernel<D, OutT, InT>;
+  CUDA_TRY(ctx, set_smem_once(kern, C::SMEM_BYTES));
   // setmaxnreg.inc waits until the registers it asks for are free within
   // the block's launch allocation: never launch a split that cannot fit.
   int regs = 0;
-  CUDA_TRY(ctx, launch_regs(fa_fwd_tc_kernel<D, OutT>, &regs));
+  CUDA_TRY(ctx, launch_regs(kern, &regs));
   if (regs * C::THREADS < C::REG_NEED)
     return fail(ctx, LLMR_ECUDA, "fa_fwd_tc: %d launch registers per thread are too few "
                 "for the register split", regs);
@@ -205,25 +233,53 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   p.seq_off[0] = 0;
   for (int i = 0; i <= p.nseq && p.nseq > 0; i++) p.seq_off[i] = seq_off[i];
   const dim3 grid = fa_grid<D>(p, B, ctx->num_sms);
-  if (!pdl) {
-    fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p);
+  FusedPro fp;
+  memset(&fp, 0, sizeof fp);
+  if (fused) {
+    fp = *fused;
+    // The start-up phase writes K'/V' of every (b, h) the first round of
+    // units touches (units are ordered by (b, h)).
+    const int first_round = (int)grid.x < p.units ? (int)grid.x : p.units;
+    fp.startup_bh = (first_round - 1) / p.nqt + 1;
+  }
+  if (!pdl && !fused) {
+    kern<<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, p, fp);
     return after_launch(ctx, "fa_fwd_tc");
   }
-  // Right behind the prologue on the same stream: programmatic dependent
-  // launch lets this grid's CTAs start (barrier init, TMEM allocation) on SMs
-  // the prologue has left; the kernel waits for the prologue's results.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(C::THREADS);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = ctx->stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  if (fused) {
+    // CTAs wait for prologue pieces written by other CTAs: all must be
+    // resident at once, which a cooperative launch guarantees (one CTA per
+    // SM at most).
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    // Right behind the prologue on the same stream: programmatic dependent
+    // launch lets this grid's CTAs start (barrier init, TMEM allocation) on
+    // SMs the prologue has left; the kernel waits for the prologue's results.
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, fa_fwd_tc_kernel<D, OutT>, mq, mk, mv, p));
-  return after_launch(ctx, "fa_fwd_tc");
+  CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, mq, mk, mv, p, fp));
+  return after_launch(ctx, fused ? "fa_fwd_tc(fused prologue)" : "fa_fwd_tc");
+}
+
+template <int D, typename InT>
+int launch_fa_fused_t(llmr_ctx *ctx, llmr_dtype od, const CUtensorMap &mq, const CUtensorMap &mk,
+                      const CUtensorMap &mv, int B, int H, int S, float scale, void *o,
+                      long long o_rs, long long o_bs, float *lse, const FusedPro &fp) {
+#define LLMR_FU_ARGS ctx, mq, mk, mv, B, H, S, S, scale, o, o_rs, o_bs, lse, 0, 0, nullptr, false, &fp
+  if (od == LLMR_F32) return launch_fa_tc<D, float, InT>(LLMR_FU_ARGS);
+  if (od == LLMR_F16) return launch_fa_tc<D, __half, InT>(LLMR_FU_ARGS);
+  return launch_fa_tc<D, __nv_bfloat16, InT>(LLMR_FU_ARGS);
+#undef LLMR_FU_ARGS
 }
 
 int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
@@ -241,6 +297,14 @@ int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
   if (od == LLMR_F16) return launch_fa_tc<64, __half>(LLMR_FA_ARGS, 0, nseq, seq_off, pdl);
   return launch_fa_tc<64, __nv_bfloat16>(LLMR_FA_ARGS, 0, nseq, seq_off, pdl);
 #undef LLMR_FA_ARGS
+}
+
+// LLMR_SEPARATE_PROLOGUE runs the prologue as its own kernel before the
+// attention kernel even where the attention kernel could run it itself (for
+// comparisons).
+bool separate_prologue() {
+  static const bool v = getenv("LLMR_SEPARATE_PROLOGUE") != nullptr;
+  return v;
 }
 
 // LLMR_NO_PDL launches the attention kernel after the prologue without
@@ -291,6 +355,52 @@ int launch_prologue(llmr_ctx *ctx, int D, llmr_dtype in, const void *q, const vo
 #undef PRO_CASE
 }
 
+unsigned grid_for(llmr_ctx *ctx, long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  const long long cap = (long long)ctx->num_sms * 16;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+// LLMR_EXACT_SIMT keeps the exact path on the SIMT kernel even where the
+// tensor-core (3xTF32) kernel applies (for comparisons).
+bool exact_simt_forced() {
+  static const bool v = getenv("LLMR_EXACT_SIMT") != nullptr;
+  return v;
+}
+
+// Exact attention on the tensor cores (D = 64): q, k, v dense fp32
+// [B][H][S][D]; res: 3 * B*H*S*D floats of workspace for their TF32
+// residuals (written here by tf32_residual_kernel).
+int launch_exact_tc(llmr_ctx *ctx, const float *q, const float *k, const float *v, float *res,
+                    const ExactParams &ep) {
+  using C = ExactTcCfg;
+  const int D = C::D, B = ep.B, H = ep.H, S = ep.S;
+  const long long n = (long long)B * H * S * D;
+  tf32_residual_kernel<<<grid_for(ctx, 3 * n, 256), 256, 0, ctx->stream>>>(q, k, v, res, n);
+  int rc = after_launch(ctx, "tf32_residual");
+  if (rc) return rc;
+  const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
+  CUtensorMap mq, mk, mv, mqr, mkr, mvr;
+  if ((rc = make_map_f32(ctx, &mq, q, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mk, k, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mv, v, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mqr, res, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mkr, res + n, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mvr, res + 2 * n, D, S, H, B, rs, hs, bs))) return rc;
+  CUDA_TRY(ctx, set_smem_once(attn_exact_tc_kernel, C::SMEM_BYTES));
+  dim3 grid((S + C::BM - 1) / C::BM, B * H);
+  attn_exact_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, mqr, mkr,
+                                                                         mvr, ep, ctx->d_err);
+  return after_launch(ctx, "attn_exact_tc");
+}
+
+bool exact_tc_applies(int D, const void *q, const void *k, const void *v) {
+  auto al = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+  return D == 64 && al(q) && al(k) && al(v) && !exact_simt_forced();
+}
+
 int launch_exact(llmr_ctx *ctx, int D, const float *q, const float *k, const float *v,
                  const ExactParams &ep) {
   const int rows_per_cta = D == 128 ? 16 : 32;
@@ -302,13 +412,6 @@ int launch_exact(llmr_ctx *ctx, int D, const float *q, const float *k, const flo
   return after_launch(ctx, "attn_exact_f32");
 }
 
-unsigned grid_for(llmr_ctx *ctx, long long n, int threads) {
-  long long b = (n + threads - 1) / threads;
-  const long long cap = (long long)ctx->num_sms * 16;
-  if (b > cap) b = cap;
-  if (b < 1) b = 1;
-  return (unsigned)b;
-}
 
 size_t dtype_size(llmr_dtype t) { return t == LLMR_F32 ? 4 : 2; }
 
@@ -511,6 +614,12 @@ int llmr_ctx_create(int device, size_t workspace_bytes, void *stream, llmr_ctx *
     llmr_ctx_destroy(c);
     return LLMR_ENOMEM;
   }
+  // One counter per (b, h) (batch * n_heads <= 65535) plus the CTA count.
+  if (cudaMalloc(&c->d_sync, kSyncInts * sizeof(int)) != cudaSuccess ||
+      cudaMemset(c->d_sync, 0, kSyncInts * sizeof(int)) != cudaSuccess) {
+    llmr_ctx_destroy(c);
+    return LLMR_ENOMEM;
+  }
   if (workspace_bytes && cudaMalloc(&c->ws, workspace_bytes) != cudaSuccess) {
     llmr_ctx_destroy(c);
     return LLMR_ENOMEM;
@@ -526,6 +635,7 @@ int llmr_ctx_destroy(llmr_ctx *ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->d_err) cudaFree(ctx->d_err);
+  if (ctx->d_sync) cudaFree(ctx->d_sync);
   for (cudaEvent_t &e : ctx->prof_ev)
     if (e) cudaEventDestroy(e);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
@@ -798,7 +908,8 @@ int llmr_out_project(llmr_ctx *ctx, const llmr_proj_desc *d, const void *o, cons
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {
   if (!d) return 0;
   const size_t n = (size_t)d->batch * d->n_heads * d->seq_len * d->head_dim;
-  if (d->flags & LLMR_EXACT) return 3 * n * 4;
+  // fp32 Q, K, V; for D = 64 also their TF32 residuals (tensor-core path).
+  if (d->flags & LLMR_EXACT) return (d->head_dim == 64 ? 6 : 3) * n * 4;
   if (d->in_dtype == LLMR_F16 && !(d->flags & (LLMR_NORM_Q | LLMR_NORM_K | LLMR_ROPE))) return 0;
   return 3 * n * 2;
 }
@@ -922,7 +1033,9 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     ep.o_row_stride = o_rs;
     ep.o_head_stride = D;
     ep.lse = lse_out;
-    if (!wide)
+    if (!wide && exact_tc_applies(D, w, w + plane, w + 2 * plane))
+      rc = launch_exact_tc(ctx, w, w + plane, w + 2 * plane, w + 3 * plane, ep);
+    else if (!wide)
       rc = launch_exact(ctx, D, w, w + plane, w + 2 * plane, ep);
     else if (D == 512)
       rc = launch_exact_wide_t<512>(ctx, w, w + plane, w + 2 * plane, ep);
@@ -944,6 +1057,49 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     if ((rc = make_map(ctx, &mv, v, D, S_kv, H, B, vs[1], vs[2], vs[0]))) return rc;
   } else {
     __half *w = static_cast<__half *>(ctx->ws);
+    // 16-bit inputs with 16-byte aligned rows: the prologue runs inside the
+    // attention kernel (one launch).
+    auto al = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
+    auto st8 = [](const long long *st) { return st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0; };
+    const bool fused = !wide && nseq == 0 && d->in_dtype != LLMR_F32 && al(q) && al(k) &&
+                       al(v) && st8(qs) && st8(ks) && st8(vs) && al(pp.q_gain) &&
+                       al(pp.k_gain) && al(pp.cos_t) && al(pp.sin_t) &&
+                       (long long)B * H < (long long)kSyncInts && !separate_prologue();
+    if (fused) {
+      const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
+      if ((rc = make_map(ctx, &mq, w, D, S, H, B, rs, hs, bs))) return rc;
+      if ((rc = make_map(ctx, &mk, w + plane, D, S, H, B, rs, hs, bs))) return rc;
+      if ((rc = make_map(ctx, &mv, w + 2 * plane, D, S, H, B, rs, hs, bs))) return rc;
+      FusedPro fp;
+      memset(&fp, 0, sizeof fp);
+      fp.q = q;
+      fp.k = k;
+      fp.v = v;
+      for (int i = 0; i < 3; i++) {
+        fp.qs[i] = qs[i];
+        fp.ks[i] = ks[i];
+        fp.vs[i] = vs[i];
+      }
+      fp.ws = w;
+      fp.sync = ctx->d_sync;
+      fp.pp = pp;
+      fp.nrb = (S + 31) / 32;
+      mark(1);
+      const bool bf = d->in_dtype == LLMR_BF16;
+      if (D == 128)
+        rc = bf ? launch_fa_fused_t<128, __nv_bfloat16>(ctx, d->out_dtype, mq, mk, mv, B, H, S,
+                                                        d->scale, o, o_rs, o_bs, lse_out, fp)
+                : launch_fa_fused_t<128, __half>(ctx, d->out_dtype, mq, mk, mv, B, H, S,
+                                                 d->scale, o, o_rs, o_bs, lse_out, fp);
+      else
+        rc = bf ? launch_fa_fused_t<64, __nv_bfloat16>(ctx, d->out_dtype, mq, mk, mv, B, H, S,
+                                                       d->scale, o, o_rs, o_bs, lse_out, fp)
+                : launch_fa_fused_t<64, __half>(ctx, d->out_dtype, mq, mk, mv, B, H, S,
+                                                d->scale, o, o_rs, o_bs, lse_out, fp);
+      mark(2);
+      ctx->prof_valid = ctx->prof_on && rc == LLMR_OK;
+      return rc;
+    }
     rc = wide ? launch_wide_cast<__half>(ctx, d->in_dtype, q, k, v, qs, ks, vs, w, B, H, S, D)
               : launch_prologue<__half>(ctx, D, d->in_dtype, q, k, v, qs, ks, vs, w, pp);
     if (rc) return rc;
@@ -1080,6 +1236,10 @@ int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k, const 
   ep.o_row_stride = head_dim;                      // [H, S, D] output
   ep.o_head_stride = (long long)seq_len * head_dim;
   ep.lse = nullptr;
+  // Tensor cores (3xTF32) when the context workspace holds the residuals.
+  const size_t res_bytes = (size_t)3 * n_heads * seq_len * head_dim * 4;
+  if (exact_tc_applies((int)head_dim, q, k, v) && ctx->ws_bytes >= res_bytes)
+    return launch_exact_tc(ctx, q, k, v, static_cast<float *>(ctx->ws), ep);
   return launch_exact(ctx, (int)head_dim, q, k, v, ep);
 }
 

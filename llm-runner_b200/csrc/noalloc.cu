@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <string.h>
 
 #include <mutex>
 
@@ -171,7 +172,9 @@ int attention(cudaStream_t st, int num_sms, const CUtensorMap &mq, const CUtenso
   p.nseq = 0;
   p.seq_off[0] = 0;
   const dim3 grid = fa_grid<D>(p, B, num_sms);
-  fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(mq, mk, mv, p);
+  FusedPro none;  // the prologue ran as its own kernel
+  memset(&none, 0, sizeof none);
+  fa_fwd_tc_kernel<D, OutT><<<grid, C::THREADS, C::SMEM_BYTES, st>>>(mq, mk, mv, p, none);
   return cudaGetLastError() == cudaSuccess ? LLMR_OK : LLMR_ECUDA;
 }
 

@@ -187,6 +187,147 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// 16-byte global -> shared copy that bypasses L1 and completes
+// asynchronously (commit / wait groups); src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// The prologue arithmetic of prologue_kernel for one lane's slice of one row
+// (lane `sub` of the row's 8 lanes; token s of tensor t = 0 Q, 1 K, 2 V) with
+// the input already widened to fp32 in x (zeros for s >= S): RMSNorm in fp32
+// with the same operation order, the interleaved RoPE rotation, fp16 RNE
+// store to dst (the row's fp16 workspace slice). Whole warps only (the norm's
+// shuffles); `t` is warp-uniform. Gains and tables 16-byte aligned.
+template <int D>
+__device__ __forceinline__ void pro_row_finish(float (&x)[D / kProLanesPerRow],
+                                               const ProParams &p, int t, int s, int sub,
+                                               __half *dst) {
+  constexpr int E = D / kProLanesPerRow;
+  const bool in = s < p.S;
+  const float *gain = t == 0 ? p.q_gain : (t == 1 ? p.k_gain : nullptr);
+  const long long grow = (long long)p.rope_row_offset + s;  // global token index
+  if (gain != nullptr) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int e = 0; e < E; e++) ss = __fmaf_rn(x[e], x[e], ss);
+#pragma unroll
+    for (int o = kProLanesPerRow / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rms = rsqrtf(ss / (float)D + p.eps);
+    const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + sub * E;
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      const float4 gv = __ldg(reinterpret_cast<const float4 *>(g + e));
+      x[e] = __fmul_rn(__fmul_rn(x[e], rms), gv.x);
+      x[e + 1] = __fmul_rn(__fmul_rn(x[e + 1], rms), gv.y);
+      x[e + 2] = __fmul_rn(__fmul_rn(x[e + 2], rms), gv.z);
+      x[e + 3] = __fmul_rn(__fmul_rn(x[e + 3], rms), gv.w);
+    }
+  }
+  if (t < 2 && p.cos_t != nullptr && in) {
+    const float *ct = p.cos_t + grow * (D / 2) + sub * (E / 2);
+    const float *st = p.sin_t + grow * (D / 2) + sub * (E / 2);
+#pragma unroll
+    for (int e = 0; e < E / 2; e += 4) {
+      const float4 cv = __ldg(reinterpret_cast<const float4 *>(ct + e));
+      const float4 sv = __ldg(reinterpret_cast<const float4 *>(st + e));
+      const float c4[4] = {cv.x, cv.y, cv.z, cv.w}, s4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float x0 = x[2 * (e + u)], x1 = x[2 * (e + u) + 1];
+        x[2 * (e + u)] = __fsub_rn(__fmul_rn(x0, c4[u]), __fmul_rn(x1, s4[u]));
+        x[2 * (e + u) + 1] = __fadd_rn(__fmul_rn(x0, s4[u]), __fmul_rn(x1, c4[u]));
+      }
+    }
+  }
+  if (in) {
+#pragma unroll
+    for (int c = 0; c < E / 8; c++) {
+      Pack<__half, 8> po;
+#pragma unroll
+      for (int e = 0; e < 8; e++) po.v[e] = __float2half_rn(x[c * 8 + e]);
+      *reinterpret_cast<Pack<__half, 8> *>(dst + c * 8) = po;
+    }
+  }
+}
+
+// Strided view selection by value (a reference into a parameter block would
+// force it into local memory): base / strides of tensor t.
+template <typename InT>
+struct ViewSel {
+  const InT *base;
+  long long bs, rs, hs;
+  __device__ __forceinline__ ViewSel(const View<InT> &vq, const View<InT> &vk,
+                                     const View<InT> &vv, int t)
+      : base(t == 0 ? vq.base : (t == 1 ? vk.base : vv.base)),
+        bs(t == 0 ? vq.bs : (t == 1 ? vk.bs : vv.bs)),
+        rs(t == 0 ? vq.rs : (t == 1 ? vk.rs : vv.rs)),
+        hs(t == 0 ? vq.hs : (t == 1 ? vk.hs : vv.hs)) {}
+};
+
+// Address of the fp16 workspace [3][B][H][S][D] row (t, b, h, s), lane slice.
+template <int D>
+__device__ __forceinline__ __half *pro_dst(__half *ws, const ProParams &p, int t, int b, int h,
+                                           int s, int sub) {
+  return ws + (((long long)t * p.B + b) * p.H + h) * (long long)p.S * D + (long long)s * D +
+         sub * (D / kProLanesPerRow);
+}
+
+// One prologue piece for the attention kernel's fused prologue: token rows
+// [s0, s0 + 32) of tensor t of (b, h) into the fp16 workspace, by one whole
+// warp (8 lanes per row, 4 rows per step), the loads of NB steps issued
+// before any is used. Inputs 16-byte aligned with strides in whole 16-byte
+// units (checked on the host).
+template <int D, typename InT, int NB>
+__device__ __forceinline__ void pro_piece(const View<InT> &vq, const View<InT> &vk,
+                                          const View<InT> &vv, __half *ws,
+                                          const ProParams &p, int t, int b, int h, int s0,
+                                          int lane) {
+  constexpr int E = D / kProLanesPerRow;
+  constexpr int VIN = 16 / sizeof(InT);
+  constexpr int CH = E / VIN;
+  constexpr int STEPS = 32 / kProRowsPerWarpStep;  // 8
+  static_assert(STEPS % NB == 0, "steps per batch");
+  const int sub = lane & (kProLanesPerRow - 1);
+  const int r = lane / kProLanesPerRow;
+  const ViewSel<InT> v(vq, vk, vv, t);
+  const InT *src0 = v.base + (long long)b * v.bs + (long long)h * v.hs + sub * E;
+#pragma unroll 1
+  for (int st0 = 0; st0 < STEPS; st0 += NB) {
+    Pack<InT, VIN> raw[NB][CH];
+#pragma unroll
+    for (int i = 0; i < NB; i++) {
+      const int s = s0 + (st0 + i) * kProRowsPerWarpStep + r;
+      if (s < p.S) {
+        const InT *src = src0 + (long long)s * v.rs;
+#pragma unroll
+        for (int c = 0; c < CH; c++)
+          raw[i][c] = *reinterpret_cast<const Pack<InT, VIN> *>(src + c * VIN);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NB; i++) {
+      const int s = s0 + (st0 + i) * kProRowsPerWarpStep + r;
+      const bool in = s < p.S;
+      float x[E];
+#pragma unroll
+      for (int c = 0; c < CH; c++)
+#pragma unroll
+        for (int e = 0; e < VIN; e++) x[c * VIN + e] = in ? to_f32<InT>(raw[i][c].v[e]) : 0.0f;
+      pro_row_finish<D>(x, p, t, s, sub, pro_dst<D>(ws, p, t, b, h, in ? s : 0, sub));
+    }
+  }
+}
+
 // Prologue of the wide-head path (D = 384 / 512, the VAE attention, which has
 // no norm or RoPE): Q, K, V from strided views of any input type to dense
 // [3][B][H][S][D] OutT (fp16 RNE for the tensor-core kernel, fp32 for the

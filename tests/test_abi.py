@@ -89,7 +89,10 @@ def test_workspace_sizes():
     raw = L.AttnConfig(n_heads=16, head_dim=64, scale=0.125)
     assert L.workspace_bytes(L.make_desc(raw, 1, 1370, L.F16, L.F16)) == 0
     ex = L.AttnConfig(n_heads=4, head_dim=64, scale=0.125, exact=True)
-    assert L.workspace_bytes(L.make_desc(ex, 1, 256, L.F32, L.F32)) == 3 * 4 * 256 * 64 * 4
+    # fp32 Q, K, V and, for the tensor-core path (D = 64), their TF32 residuals
+    assert L.workspace_bytes(L.make_desc(ex, 1, 256, L.F32, L.F32)) == 6 * 4 * 256 * 64 * 4
+    ex128 = L.AttnConfig(n_heads=4, head_dim=128, scale=0.088, exact=True)
+    assert L.workspace_bytes(L.make_desc(ex128, 1, 256, L.F32, L.F32)) == 3 * 4 * 256 * 128 * 4
     vae = L.AttnConfig(n_heads=1, head_dim=512, scale=512 ** -0.5)
     assert L.workspace_bytes(L.make_desc(vae, 1, 16384, L.F32, L.F32)) == 3 * 16384 * 512 * 2
     assert L.workspace_bytes(L.make_desc(vae, 1, 16384, L.F16, L.F16)) == 0

@@ -1,0 +1,105 @@
+"""GPU: exact fp32 attention (spatial_attention math) on the tensor cores,
+D = 64: three TF32 products per fp32 product (tcgen05.mma kind::tf32, fp32
+accumulation). Checked against the oracle's restatement of the reference's
+spatial_attention within the fp32 bar (1e-5 max and mean): the plumbing
+config, a Depth-Anything-shaped fp32 case (H16 S1370), ragged token counts,
+batch 2 with strided output and the LSE, and the spatial_attention mirror.
+The launch counts show which kernel ran (prologue + residuals + tensor-core
+kernel for the fused op; residuals + tensor-core kernel for the mirror)."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5
+
+
+def _t():
+    import torch
+    return torch
+
+
+def _check(got, want, what):
+    assert np.all(np.isfinite(got)), what + ": non-finite"
+    err = np.abs(got.astype(np.float64) - want.astype(np.float64))
+    assert err.max() <= TOL and err.mean() <= TOL, f"{what}: max {err.max():.3e} mean {err.mean():.3e}"
+
+
+def _exact_case(ctx, B, H, S, seed, lse=False, scale=0.125, in_scale=1.0):
+    import llmr_attn as L
+    torch = _t()
+    rng = np.random.default_rng(seed)
+    D = 64
+    q, k, v = (rng.standard_normal((B, H, S, D), dtype=np.float32) * np.float32(in_scale)
+               for _ in range(3))
+    cfg = L.AttnConfig(n_heads=H, head_dim=D, scale=scale, layout=L.BHSD, exact=True)
+    dq, dk, dv = (torch.from_numpy(a).cuda() for a in (q, k, v))
+    o = torch.full((B, S, H * D), float("nan"), device="cuda")
+    l_ = torch.full((B, H, S), float("nan"), device="cuda") if lse else None
+    ctx.reserve(L.workspace_bytes(L.make_desc(cfg, B, S, L.F32, L.F32)))
+    n0 = ctx.launches
+    L.attention_fused(ctx, dq, dk, dv, o, cfg, batch=B, seq_len=S, lse=l_)
+    ctx.sync()
+    assert ctx.launches - n0 == 3  # prologue, TF32 residuals, tensor-core attention
+    got = o.cpu().numpy()
+    for b in range(B):
+        want = O.spatial_attention(q[b], k[b], v[b], D, H, S, scale)  # [H, S, D]
+        _check(got[b].reshape(S, H, D).transpose(1, 0, 2), want, f"B{B} H{H} S{S} b={b}")
+    if lse:
+        q64, k64 = q.astype(np.float64), k.astype(np.float64)
+        s = np.einsum("bhsd,bhtd->bhst", q64, k64) * scale
+        m = s.max(-1, keepdims=True)
+        want_lse = (m[..., 0] + np.log(np.exp(s - m).sum(-1)))
+        assert np.abs(l_.cpu().numpy() - want_lse).max() <= 1e-5
+    return got
+
+
+def test_exact_tc_plumbing_config(ctx):
+    """B1 H4 S256 D64 fp32, N(0,1) seed 0, scale 1/8."""
+    from llmr_attn import configs as C
+    import llmr_attn as L
+    from llmr_attn.runner import to_device
+    prep = C.prepare(C.C1, L.rope_tables)
+    dc = to_device(prep, out_dtype="f32")
+    ctx.reserve(L.workspace_bytes(dc.desc()))
+    n0 = ctx.launches
+    dc.run(ctx)
+    ctx.sync()
+    assert ctx.launches - n0 == 3
+    got = dc.o.cpu().numpy()[0]
+    want = O.attention_block(prep.q[0], prep.k[0], prep.v[0], 4, 64, C.C1.scale, exact=True)
+    _check(got, want, "plumbing")
+
+
+def test_exact_tc_depth_shaped_fp32(ctx):
+    """Depth-Anything ViT-L shape (H16 S1370 D64) in fp32: ragged last key
+    block (1370 = 10 * 128 + 90), 0.5 * N(0, 1) inputs, scale 1/8."""
+    _exact_case(ctx, 1, 16, 1370, seed=1, in_scale=0.5)
+
+
+@pytest.mark.parametrize("S", [1, 5, 127, 129, 300, 1000])
+def test_exact_tc_ragged(ctx, S):
+    _exact_case(ctx, 1, 2, S, seed=100 + S)
+
+
+def test_exact_tc_batch_lse_and_peaky_rows(ctx):
+    # Larger scale: peaky rows exercise the lazy rescale (max jumps > 2^8).
+    _exact_case(ctx, 2, 3, 700, seed=7, lse=True, scale=0.6)
+
+
+def test_spatial_attention_mirror_tensor_cores(ctx):
+    import llmr_attn as L
+    torch = _t()
+    H, S, D = 3, 517, 64
+    rng = np.random.default_rng(11)
+    q, k, v = (rng.standard_normal((H, S, D), dtype=np.float32) for _ in range(3))
+    o = torch.full((H, S, D), float("nan"), device="cuda")
+    ctx.reserve(3 * H * S * D * 4)
+    n0 = ctx.launches
+    L.spatial_attention(ctx, *(torch.from_numpy(a).cuda() for a in (q, k, v)), None, o, D, H, S,
+                        0.125)
+    ctx.sync()
+    assert ctx.launches - n0 == 2  # TF32 residuals + tensor-core attention
+    _check(o.cpu().numpy(), O.spatial_attention(q, k, v, D, H, S, 0.125), "mirror")
