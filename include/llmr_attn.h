@@ -86,6 +86,14 @@ int llmr_set_stream(llmr_ctx *ctx, void *stream);
  * NCCL send/receive kernels of the sequence-sharded ring. No reference
  * counterpart (the reference is single-GPU). */
 int llmr_ctx_set_sm_budget(llmr_ctx *ctx, int sms);
+/* Diagnostic builds only (compiled with -DLLMR_TIMELINE, `make TIMELINE=1`):
+ * the D <= 128 attention kernel records per-CTA event timestamps
+ * (%globaltimer ns; 32 slots per CTA, the slot meanings are listed in
+ * csrc/fa_tc.cuh) into `device_buffer` (>= num_sms * 32 * 8 bytes; NULL
+ * turns it off). Other builds return LLMR_EINVAL. No reference counterpart
+ * (the reference's timer is per dispatch, dependencies/zimage.c3l/
+ * dit.c3:17-26). */
+int llmr_timeline_set(llmr_ctx *ctx, void *device_buffer, size_t bytes);
 void *llmr_get_stream(llmr_ctx *ctx);
 const char *llmr_last_error(llmr_ctx *ctx);
 /* Wait for all work on the context stream; reports device-side timeouts.
@@ -192,8 +200,9 @@ int llmr_mrope(llmr_ctx *ctx, float *data, const float *cos_t,
  * signature compatibility and ignored (may be NULL): no S x S buffer is
  * materialised. head_dim 64 or 128. head_dim 64 runs on the tensor cores
  * (three TF32 products per fp32 product, fp32 accumulation) when the
- * context workspace holds 3*n_heads*seq_len*64*4 bytes (llmr_ctx_reserve)
- * for the operands' TF32 residuals; otherwise, and for head_dim 128, on an
+ * context workspace holds 4*n_heads*64*(2*seq_len + 2*ceil4(seq_len)) bytes
+ * (llmr_ctx_reserve; ceil4 rounds up to a multiple of 4) for the operands'
+ * TF32 residuals and V transposed; otherwise, and for head_dim 128, on an
  * fp32 FMA kernel. Both stay within 1e-5 of the reference's arithmetic. */
 int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k,
                            const float *v, float *scores, float *o,

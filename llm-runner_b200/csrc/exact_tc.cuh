@@ -9,12 +9,13 @@
 // with a relative error near 2^-20 (the dropped r*r term and the truncation
 // of r), accumulated in fp32 in TMEM. The raw fp32 tensors serve as t(x)
 // directly (the MMA truncates them); r(x) comes from a small kernel
-// (tf32_residual_kernel) for Q, K and V, and from the softmax threads for P.
+// (tf32_prepare_kernel, which also transposes V: kind::tf32 takes no
+// MN-major shared-memory operand) and from the softmax threads for P.
 //
 // CTA = 128 query rows of one (b, h); 192 threads:
 //   warps 0-3  softmax (thread i owns query row i = TMEM lane i)
 //   warp  4    TMA producer: Q and r(Q) once, then per 128-key block
-//              K, r(K), V, r(V) into four 32 KB slots
+//              K, r(K), V^T, r(V)^T into four 32 KB slots
 //   warp  5    TMEM owner and MMA issuer (one elected lane)
 // TMEM (512 columns): S0 [0,128) S1 [128,256) r(P) [256,384) O [384,448).
 // S_j lands in buffer j&1 while the softmax works on the other one; the
@@ -64,15 +65,40 @@ __device__ __forceinline__ float tf32_residual(float x) {
   return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
 }
 
-// dst[t * n + i] = tf32_residual(src_t[i]) for t = 0, 1, 2 (Q, K, V).
-__global__ void tf32_residual_kernel(const float *q, const float *k, const float *v, float *dst,
-                                     long long n) {
-  const long long total = 3 * n;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-       i += (long long)gridDim.x * blockDim.x) {
-    const long long t = i / n, j = i - t * n;
-    const float *src = t == 0 ? q : (t == 1 ? k : v);
-    dst[i] = tf32_residual(src[j]);
+// Operand preparation for the tensor-core exact kernel, dense fp32
+// [B*H][S][D] inputs: qr, kr = TF32 residuals of Q and K (same layout);
+// vt, vtr = V and its residual transposed to [B*H][D][Sp] (keys contiguous,
+// Sp = S rounded up to a multiple of 4 so rows are 16-byte aligned). The
+// P.V product needs V as a K-major operand: kind::tf32 takes no MN-major
+// (transposed) shared-memory operand. Grid (ceil(S/32), D/32, B*H), 32 x 8
+// threads: one 32 x 32 tile each, transposed through shared memory.
+__global__ void __launch_bounds__(256)
+    tf32_prepare_kernel(const float *q, const float *k, const float *v, float *qr, float *kr,
+                        float *vt, float *vtr, int S, int Sp, int D) {
+  __shared__ float tile[32][33];
+  const long long bh = blockIdx.z;
+  const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const long long base = bh * S * D;
+  for (int r = ty; r < 32; r += 8) {
+    const int s = s0 + r;
+    if (s < S) {
+      const long long i = base + (long long)s * D + d0 + tx;
+      qr[i] = tf32_residual(q[i]);
+      kr[i] = tf32_residual(k[i]);
+      tile[r][tx] = v[i];
+    }
+  }
+  __syncthreads();
+  const long long tbase = bh * D * Sp;
+  for (int r = ty; r < 32; r += 8) {
+    const int s = s0 + tx;
+    if (s < S) {
+      const float x = tile[tx][r];
+      const long long o = tbase + (long long)(d0 + r) * Sp + s;
+      vt[o] = x;
+      vtr[o] = tf32_residual(x);
+    }
   }
 }
 
@@ -83,7 +109,8 @@ struct ExactTcCfg {
   static constexpr int CHUNK = 128 * 128;          // 32 fp32 columns x 128 rows, SW128
   static constexpr int TILE = BM * D * 4;          // one fp32 tile of 128 rows (32 KB)
   static constexpr int Q_OFF = 0;                  // Q, r(Q)
-  static constexpr int KV_OFF = 2 * TILE;          // slots: K, r(K), V, r(V)
+  static constexpr int KV_OFF = 2 * TILE;          // slots: K, r(K), V^T, r(V)^T
+  static constexpr int VCHUNK = 64 * 128;          // 32 keys x 64 d-rows of V^T, SW128
   static constexpr int BAR_OFF = KV_OFF + 4 * TILE;
   // barriers: q_full, kv_full[4], kv_empty[4], s_full[2], p_full, pv_done,
   // drain; then tmem base word and abort flag
@@ -99,8 +126,9 @@ struct ExactTcCfg {
 // Lazy-max threshold (log2 units): P <= 2^8 between rescales.
 constexpr float kExactMaxExp = 8.0f;
 
-// Maps (fp32, 4-D (d, s, h, b), 32 x 128 boxes, SW128): tmQ/tmK/tmV the
-// operands, tmQr/tmKr/tmVr their TF32 residuals.
+// Maps (fp32, SW128): tmQ/tmK and their residuals tmQr/tmKr over (d, s, h, b)
+// with 32 x 128 boxes; tmV/tmVr over V^T and its residual, (s, d, h, b) with
+// 32 x 64 boxes.
 __global__ void __launch_bounds__(192, 1)
     attn_exact_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                          const __grid_constant__ CUtensorMap tmK,
@@ -118,7 +146,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *sKV = smem + C::KV_OFF;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
   uint64_t *q_full = bars;
-  uint64_t *kv_full = bars + 1;     // [slot]: 0 K, 1 r(K), 2 V, 3 r(V)
+  uint64_t *kv_full = bars + 1;     // [slot]: 0 K, 1 r(K), 2 V^T, 3 r(V)^T
   uint64_t *kv_empty = kv_full + 4;
   uint64_t *s_full = kv_empty + 4;  // [buffer]
   uint64_t *p_full = s_full + 2;
@@ -176,9 +204,15 @@ __global__ void __launch_bounds__(192, 1)
             break;
           }
           mbar_arrive_expect_tx(&kv_full[s], C::TILE);
-          for (int c = 0; c < D / 32; c++)
-            tma_load_4d(sKV + s * C::TILE + c * C::CHUNK, maps[s], &kv_full[s], c * 32,
-                        j * C::BN, h, b);
+          if (s < 2) {  // K rows: 2 chunks of 32 d-columns
+            for (int c = 0; c < D / 32; c++)
+              tma_load_4d(sKV + s * C::TILE + c * C::CHUNK, maps[s], &kv_full[s], c * 32,
+                          j * C::BN, h, b);
+          } else {  // V^T rows (d): 4 chunks of 32 keys
+            for (int c = 0; c < C::BN / 32; c++)
+              tma_load_4d(sKV + s * C::TILE + c * C::VCHUNK, maps[s], &kv_full[s],
+                          j * C::BN + c * 32, 0, h, b);
+          }
           armed[s] = j + 1;
         }
       }
@@ -190,7 +224,7 @@ __global__ void __launch_bounds__(192, 1)
   } else if (warp == 5) {
     // ------------------------------------------------------- MMA issuer
     constexpr uint32_t IDESC_S = idesc_tf32(128, C::BN, 0);
-    constexpr uint32_t IDESC_O = idesc_tf32(128, D, 1);
+    constexpr uint32_t IDESC_O = idesc_tf32(128, D, 0);  // V^T: K-major
     const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
     // S_buf = Q K^T + Q r(K)^T + r(Q) K^T over D (8 steps of K = 8 each).
     auto issue_s = [&](int buf) {
@@ -207,7 +241,8 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     };
-    // O (+)= P V + P r(V) + r(P) V over the block's 128 keys (16 steps of 8).
+    // O (+)= P V + P r(V) + r(P) V over the block's 128 keys (16 steps of 8);
+    // V^T is the K-major B operand (rows d, keys contiguous).
     auto issue_pv = [&](int buf, bool acc) {
 #pragma unroll
       for (int pass = 0; pass < 3; pass++) {
@@ -215,9 +250,10 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t va = sKVa + (pass == 1 ? 3 : 2) * C::TILE;
 #pragma unroll
         for (int ks = 0; ks < C::BN / 8; ks++) {
+          const uint32_t off = (ks >> 2) * C::VCHUNK + (ks & 3) * 32;
           if (elect_one())
-            mma_ts_tf32(tmem + C::O_COL, pa + ks * 8, sdesc_sw128(va + ks * 1024, C::CHUNK, 1024),
-                        IDESC_O, (acc || pass > 0 || ks > 0) ? 1u : 0u);
+            mma_ts_tf32(tmem + C::O_COL, pa + ks * 8, sdesc_sw128(va + off, 16, 1024), IDESC_O,
+                        (acc || pass > 0 || ks > 0) ? 1u : 0u);
         }
       }
     };

@@ -52,7 +52,28 @@ struct FaParams {
   int merge;             // o (fp32) and lse hold a partial result over other
                          // keys: merge into them by log-sum-exp
   int *err;              // device error word (nonzero on timeout)
+  // Per-CTA event timestamps (globaltimer ns, kTimelineSlots per CTA) when
+  // the library is built with -DLLMR_TIMELINE and a buffer is set; else null.
+  unsigned long long *timeline;
 };
+
+// Timeline slots (LLMR_TIMELINE builds): 0 kernel start, 1 start-up phase
+// done, 2 + 2k / 3 + 2k producer begins unit k / its K'/V' are ready (k < 4),
+// 10 + 2k / 11 + 2k tile 0's first S of unit k ready / epilogue done,
+// 18 background Q' of unit 1 done, 19 background K'/V' pieces done,
+// 20 background done, 21 kernel end.
+constexpr int kTimelineSlots = 32;
+#ifdef LLMR_TIMELINE
+#define LLMR_TL(slot)                                                                    \
+  do {                                                                                   \
+    if (p.timeline)                                                                      \
+      p.timeline[(size_t)blockIdx.x * kTimelineSlots + (slot)] = globaltimer_ns();       \
+  } while (0)
+#else
+#define LLMR_TL(slot) \
+  do {                \
+  } while (0)
+#endif
 
 // The prologue fused into the attention kernel (the fused op's default for
 // 16-bit inputs): the kernel itself writes the fp16 Q', K', V' its TMA maps
@@ -339,6 +360,7 @@ __global__ void __launch_bounds__(384, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_base_slot;
+  if (threadIdx.x == 0) LLMR_TL(0);
   // Launched right behind the prologue (programmatic dependent launch), the
   // set-up above overlaps its tail; its output is read only after this.
   griddep_wait();
@@ -379,6 +401,7 @@ __global__ void __launch_bounds__(384, 1)
       fence_proxy_async_global();
     }
     __syncthreads();
+    if (threadIdx.x == 0) LLMR_TL(1);
   }
 
   if (warp >= 8) {
@@ -398,6 +421,7 @@ __global__ void __launch_bounds__(384, 1)
           const int b = un.b, h = un.h, nblk = un.nblk;
           // Q of this unit may replace the previous unit's once its last
           // S MMAs have completed.
+          if (k < 4) LLMR_TL(2 + 2 * k);
           if (k > 0 && !mbar_wait(q_empty, (k - 1) & 1, abort_flag)) {
             ok = false;
             break;
@@ -416,6 +440,7 @@ __global__ void __launch_bounds__(384, 1)
             }
             fence_proxy_async_global();
           }
+          if (k < 4) LLMR_TL(3 + 2 * k);
           mbar_arrive_expect_tx(q_full, 2 * C::TILE_BYTES);
           for (int t = 0; t < 2; t++)
             for (int c = 0; c < C::NCHUNK; c++)
@@ -634,15 +659,18 @@ __global__ void __launch_bounds__(384, 1)
         if ((g & 7) == 7) {  // piece complete
           if (c.k < 0) {
             publish(c.b * p.H + c.h);
+            if ((g >> 3) == nq1 + nkv - 1 && warp == 10 && lane == 0) LLMR_TL(19);
           } else if (c.j == 3) {  // the warp's last Q' piece of unit k
             fence_proxy_async_global();
             __threadfence();
             __syncwarp();
             if (lane == 0) q_done[wb] = c.k;
+            if (c.k == 1 && warp == 10 && lane == 0) LLMR_TL(18);
           }
         }
       }
       cp_async_wait<0>();
+      if (warp == 10 && lane == 0) LLMR_TL(20);
     }
   } else {
     reg_alloc<C::REG_SOFTMAX>();
@@ -665,6 +693,7 @@ __global__ void __launch_bounds__(384, 1)
         const int jj = jb + j;
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], jj & 1, abort_flag));
         if (!ok) break;
+        if (j == 0 && k < 4 && threadIdx.x == 0) LLMR_TL(10 + 2 * k);
         tc_fence_after();
         const int valid = un.sk - j * C::BN;  // keys of this block inside the sequence
         // Applies the key mask (keys past the sequence -> -inf) to chunk c.
@@ -807,6 +836,7 @@ __global__ void __launch_bounds__(384, 1)
         if (qin) store_row_chunk<OutT>(dst + c * 32, v);
       }
       if (p.lse != nullptr && qin) p.lse[(long long)bh * S + qrow] = lse_out;
+      if (k < 4 && threadIdx.x == 0) LLMR_TL(11 + 2 * k);
     }
   }
 
@@ -818,6 +848,7 @@ __global__ void __launch_bounds__(384, 1)
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
   if (threadIdx.x == 0 && *abort_flag) atomicExch(p.err, 1);
+  if (threadIdx.x == 0) LLMR_TL(21);
   if constexpr (FUSED) {
     // Every wait of this CTA on the piece counters is over. The last CTA to
     // get here clears the counters for the next launch.

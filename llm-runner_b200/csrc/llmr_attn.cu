@@ -39,6 +39,7 @@ struct llmr_ctx {
   size_t ws_bytes = 0;
   int *d_err = nullptr;
   int *d_sync = nullptr;  // fused-prologue piece counters (self-resetting)
+  unsigned long long *timeline = nullptr;  // LLMR_TIMELINE builds: event buffer
   uint64_t launches = 0;
   int num_sms = 0;
   bool prof_on = false;
@@ -138,10 +139,10 @@ int make_map2d(llmr_ctx *ctx, CUtensorMap *map, const void *base, long long inne
   return LLMR_OK;
 }
 
-// 4-D fp32 tensor map over (d, s, h, b) with a 32 x 128 x 1 x 1 box and
-// 128-byte swizzle (one SW128 K-major or MN-major tf32 operand chunk).
+// 4-D fp32 tensor map over (inner, rows, h, b) with a 32 x box_rows x 1 x 1
+// box and 128-byte swizzle (one SW128 K-major tf32 operand chunk).
 int make_map_f32(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S, int H, int B,
-                 long long rs, long long hs, long long bs) {
+                 long long rs, long long hs, long long bs, int box_rows = 128) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(ctx, LLMR_ECUDA, "cuTensorMapEncodeTiled unavailable");
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((rs * 4) & 15) || ((hs * 4) & 15) ||
@@ -149,7 +150,7 @@ int make_map_f32(llmr_ctx *ctx, CUtensorMap *map, const void *base, int D, int S
     return fail(ctx, LLMR_EINVAL, "TMA operand base/strides must be 16-byte aligned");
   cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)S, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)rs * 4, (cuuint64_t)hs * 4, (cuuint64_t)bs * 4};
-  cuuint32_t box[4] = {32, 128, 1, 1};
+  cuuint32_t box[4] = {32, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void *>(base), dims,
                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -229,6 +230,7 @@ int launch_fa_tc(llmr_ctx *ctx, const CUtensorMap &mq, const CUtensorMap &mk,
   p.lse = lse;
   p.merge = merge;
   p.err = ctx->d_err;
+  p.timeline = ctx->timeline;
   p.nseq = seq_off != nullptr ? nseq : 0;
   p.seq_off[0] = 0;
   for (int i = 0; i <= p.nseq && p.nseq > 0; i++) p.seq_off[i] = seq_off[i];
@@ -299,11 +301,12 @@ int launch_fa_tc_any(llmr_ctx *ctx, int D, llmr_dtype od, const CUtensorMap &mq,
 #undef LLMR_FA_ARGS
 }
 
-// LLMR_SEPARATE_PROLOGUE runs the prologue as its own kernel before the
-// attention kernel even where the attention kernel could run it itself (for
-// comparisons).
-bool separate_prologue() {
-  static const bool v = getenv("LLMR_SEPARATE_PROLOGUE") != nullptr;
+// LLMR_FUSED_PROLOGUE=1 runs the prologue inside the attention kernel (one
+// cooperative launch) instead of as its own kernel launched ahead of it.
+// Measured slower on B200 (the start-up pieces and the background warps are
+// latency-bound and slow the softmax warps), so it is not the default.
+bool fused_prologue_enabled() {
+  static const bool v = getenv("LLMR_FUSED_PROLOGUE") != nullptr;
   return v;
 }
 
@@ -370,25 +373,36 @@ bool exact_simt_forced() {
   return v;
 }
 
+// Workspace floats the tensor-core exact kernel needs besides its inputs:
+// TF32 residuals of Q and K, and V^T with its residual (keys padded to a
+// multiple of 4 per row).
+long long exact_tc_extra_floats(long long B, long long H, long long S, long long D) {
+  const long long Sp = (S + 3) / 4 * 4;
+  return 2 * B * H * S * D + 2 * B * H * D * Sp;
+}
+
 // Exact attention on the tensor cores (D = 64): q, k, v dense fp32
-// [B][H][S][D]; res: 3 * B*H*S*D floats of workspace for their TF32
-// residuals (written here by tf32_residual_kernel).
-int launch_exact_tc(llmr_ctx *ctx, const float *q, const float *k, const float *v, float *res,
+// [B][H][S][D]; extra: exact_tc_extra_floats(...) floats of workspace.
+int launch_exact_tc(llmr_ctx *ctx, const float *q, const float *k, const float *v, float *extra,
                     const ExactParams &ep) {
   using C = ExactTcCfg;
   const int D = C::D, B = ep.B, H = ep.H, S = ep.S;
-  const long long n = (long long)B * H * S * D;
-  tf32_residual_kernel<<<grid_for(ctx, 3 * n, 256), 256, 0, ctx->stream>>>(q, k, v, res, n);
-  int rc = after_launch(ctx, "tf32_residual");
+  const int Sp = (S + 3) / 4 * 4;
+  const long long n = (long long)B * H * S * D, nt = (long long)B * H * D * Sp;
+  float *qr = extra, *kr = extra + n, *vt = extra + 2 * n, *vtr = vt + nt;
+  dim3 pgrid((S + 31) / 32, D / 32, B * H);
+  tf32_prepare_kernel<<<pgrid, 256, 0, ctx->stream>>>(q, k, v, qr, kr, vt, vtr, S, Sp, D);
+  int rc = after_launch(ctx, "tf32_prepare");
   if (rc) return rc;
   const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
+  const long long trs = Sp, ths = (long long)D * Sp, tbs = (long long)H * D * Sp;
   CUtensorMap mq, mk, mv, mqr, mkr, mvr;
   if ((rc = make_map_f32(ctx, &mq, q, D, S, H, B, rs, hs, bs))) return rc;
   if ((rc = make_map_f32(ctx, &mk, k, D, S, H, B, rs, hs, bs))) return rc;
-  if ((rc = make_map_f32(ctx, &mv, v, D, S, H, B, rs, hs, bs))) return rc;
-  if ((rc = make_map_f32(ctx, &mqr, res, D, S, H, B, rs, hs, bs))) return rc;
-  if ((rc = make_map_f32(ctx, &mkr, res + n, D, S, H, B, rs, hs, bs))) return rc;
-  if ((rc = make_map_f32(ctx, &mvr, res + 2 * n, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mqr, qr, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mkr, kr, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mv, vt, S, D, H, B, trs, ths, tbs, 64))) return rc;
+  if ((rc = make_map_f32(ctx, &mvr, vtr, S, D, H, B, trs, ths, tbs, 64))) return rc;
   CUDA_TRY(ctx, set_smem_once(attn_exact_tc_kernel, C::SMEM_BYTES));
   dim3 grid((S + C::BM - 1) / C::BM, B * H);
   attn_exact_tc_kernel<<<grid, C::THREADS, C::SMEM_BYTES, ctx->stream>>>(mq, mk, mv, mqr, mkr,
@@ -668,6 +682,22 @@ int llmr_set_stream(llmr_ctx *ctx, void *stream) {
   return LLMR_OK;
 }
 
+int llmr_timeline_set(llmr_ctx *ctx, void *device_buffer, size_t bytes) {
+  int rc = check_ctx(ctx);
+  if (rc) return rc;
+#ifdef LLMR_TIMELINE
+  if (device_buffer && bytes < (size_t)ctx->num_sms * kTimelineSlots * 8)
+    return fail(ctx, LLMR_EINVAL, "timeline buffer needs %zu bytes",
+                (size_t)ctx->num_sms * kTimelineSlots * 8);
+  ctx->timeline = static_cast<unsigned long long *>(device_buffer);
+  return LLMR_OK;
+#else
+  (void)device_buffer;
+  (void)bytes;
+  return fail(ctx, LLMR_EINVAL, "built without LLMR_TIMELINE");
+#endif
+}
+
 int llmr_ctx_set_sm_budget(llmr_ctx *ctx, int sms) {
   int rc = check_ctx(ctx);
   if (rc) return rc;
@@ -908,8 +938,11 @@ int llmr_out_project(llmr_ctx *ctx, const llmr_proj_desc *d, const void *o, cons
 size_t llmr_attention_workspace_bytes(const llmr_attn_desc *d) {
   if (!d) return 0;
   const size_t n = (size_t)d->batch * d->n_heads * d->seq_len * d->head_dim;
-  // fp32 Q, K, V; for D = 64 also their TF32 residuals (tensor-core path).
-  if (d->flags & LLMR_EXACT) return (d->head_dim == 64 ? 6 : 3) * n * 4;
+  // fp32 Q, K, V; for D = 64 also the tensor-core path's residuals and V^T.
+  if (d->flags & LLMR_EXACT)
+    return 3 * n * 4 + (d->head_dim == 64 ? (size_t)exact_tc_extra_floats(d->batch, d->n_heads,
+                                                                            d->seq_len, 64) * 4
+                                           : 0);
   if (d->in_dtype == LLMR_F16 && !(d->flags & (LLMR_NORM_Q | LLMR_NORM_K | LLMR_ROPE))) return 0;
   return 3 * n * 2;
 }
@@ -1057,14 +1090,14 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     if ((rc = make_map(ctx, &mv, v, D, S_kv, H, B, vs[1], vs[2], vs[0]))) return rc;
   } else {
     __half *w = static_cast<__half *>(ctx->ws);
-    // 16-bit inputs with 16-byte aligned rows: the prologue runs inside the
-    // attention kernel (one launch).
+    // With LLMR_FUSED_PROLOGUE, 16-bit inputs with 16-byte aligned rows run
+    // the prologue inside the attention kernel (one launch).
     auto al = [](const void *ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0; };
     auto st8 = [](const long long *st) { return st[0] % 8 == 0 && st[1] % 8 == 0 && st[2] % 8 == 0; };
     const bool fused = !wide && nseq == 0 && d->in_dtype != LLMR_F32 && al(q) && al(k) &&
                        al(v) && st8(qs) && st8(ks) && st8(vs) && al(pp.q_gain) &&
                        al(pp.k_gain) && al(pp.cos_t) && al(pp.sin_t) &&
-                       (long long)B * H < (long long)kSyncInts && !separate_prologue();
+                       (long long)B * H < (long long)kSyncInts && fused_prologue_enabled();
     if (fused) {
       const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
       if ((rc = make_map(ctx, &mq, w, D, S, H, B, rs, hs, bs))) return rc;
@@ -1237,7 +1270,7 @@ int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k, const 
   ep.o_head_stride = (long long)seq_len * head_dim;
   ep.lse = nullptr;
   // Tensor cores (3xTF32) when the context workspace holds the residuals.
-  const size_t res_bytes = (size_t)3 * n_heads * seq_len * head_dim * 4;
+  const size_t res_bytes = (size_t)exact_tc_extra_floats(1, n_heads, seq_len, head_dim) * 4;
   if (exact_tc_applies((int)head_dim, q, k, v) && ctx->ws_bytes >= res_bytes)
     return launch_exact_tc(ctx, q, k, v, static_cast<float *>(ctx->ws), ep);
   return launch_exact(ctx, (int)head_dim, q, k, v, ep);

@@ -32,7 +32,9 @@ from typing import Optional, Sequence
 import numpy as np
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "libllmr_attn.so")
+# LLMR_LIB may name another build of the same library (e.g. the diagnostic
+# timeline build, `make TIMELINE=1 OUT=...`).
+LIB_PATH = os.environ.get("LLMR_LIB") or os.path.join(os.path.dirname(_HERE), "libllmr_attn.so")
 
 OK, EINVAL, ENOMEM, ECUDA, ENCCL, ETIMEOUT, ENODEV = range(7)
 _STATUS_NAMES = {0: "LLMR_OK", 1: "LLMR_EINVAL", 2: "LLMR_ENOMEM", 3: "LLMR_ECUDA",
@@ -111,6 +113,7 @@ def _load() -> ctypes.CDLL:
         "llmr_ctx_reserve": (i32, [vp, ctypes.c_size_t]),
         "llmr_set_stream": (i32, [vp, vp]),
         "llmr_ctx_set_sm_budget": (i32, [vp, i32]),
+        "llmr_timeline_set": (i32, [vp, vp, ctypes.c_size_t]),
         "llmr_get_stream": (vp, [vp]),
         "llmr_last_error": (ctypes.c_char_p, [vp]),
         "llmr_sync": (i32, [vp]),
@@ -206,6 +209,13 @@ class Context:
 
     def reserve(self, nbytes: int) -> None:
         self.check(lib.llmr_ctx_reserve(self.handle, nbytes))
+
+    def timeline(self, buf) -> None:
+        """Diagnostic builds: per-CTA event timestamps of the attention kernel
+        into `buf` (a uint64/int64 CUDA tensor of >= num_sms * 32 elements;
+        None turns it off)."""
+        nbytes = 0 if buf is None else buf.numel() * buf.element_size()
+        self.check(lib.llmr_timeline_set(self.handle, _ptr(buf), nbytes))
 
     def set_sm_budget(self, sms: int) -> None:
         """Persistent kernels of this context use at most `sms` SMs (0 = all)."""

@@ -1,7 +1,8 @@
 """CPU: randomised models of the tensor-core kernels' mbarrier protocols —
 fa_fwd_tc_kernel (llm-runner_b200/csrc/fa_tc.cuh), the two wide-head kernels
-(fa_wide.cuh, checked against these models before their first GPU run) and
-the QKV projection's CTA-pair GEMM (qkv_proj.cuh).
+(fa_wide.cuh, checked against these models before their first GPU run), the
+QKV projection's CTA-pair GEMM (qkv_proj.cuh) and the exact fp32 kernel on
+the tensor cores (exact_tc.cuh, checked before its first GPU run).
 
 Each model runs the kernel's roles as coroutines under a random scheduler
 with random stalls: the TMA producer(s), the MMA-issuing warp, the softmax
@@ -864,6 +865,128 @@ def run_qkv_pair(seed, NST, k_blocks, tiles, p_stall=0.0, wait_acc_empty=True):
     _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q)
 
 
+def run_exact_tc(seed, nblk, p_rescale, wait_pv=True):
+    """attn_exact_tc_kernel (exact_tc.cuh): one query tile; per block j the
+    slots 0-3 hold K, r(K), V, r(V) of block j; S_j lands in TMEM buffer j&1
+    (MMA order S_0, then per block S_{j+1}, PV_j); the softmax writes P_j over
+    S_j at once, then waits for PV_{j-1} before it may rescale O and write
+    r(P_j) into the one r(P) buffer. wait_pv=False plants a bug: r(P_j)
+    written (and O rescaled) without waiting for PV_{j-1}."""
+    rng = random.Random(seed)
+    q_full = Bar("q_full", 1)
+    kv_full = [Bar(f"kv_full{i}", 1) for i in range(4)]
+    kv_empty = [Bar(f"kv_empty{i}", 1) for i in range(4)]
+    s_full = [Bar(f"s_full{b}", 1) for b in range(2)]
+    p_full, pv_done = Bar("p_full", 4), Bar("pv_done", 1)
+    slot_tag, slot_busy = [None] * 4, [False] * 4
+    q_in = [False]
+    sbuf = [[None] * 4 for _ in range(2)]  # per buffer, per warp: ("S"|"P", j)
+    pl = [None] * 4                        # r(P) buffer, per warp: j
+    o_last = [None]                        # last PV applied to O
+    tma_q, mma_q = [], []
+
+    def producer():
+        tma_q.append(("Q", 0, None, q_full))
+        yield True
+        for j in range(nblk):
+            for s_ in range(4):
+                if j > 0:
+                    yield from wait(kv_empty[s_], j - 1)
+                tma_q.append(("KV", j, s_, kv_full[s_]))
+                yield True
+
+    def mma():
+        yield from wait(q_full, 0)
+        yield from wait(kv_full[0], 0)
+        yield from wait(kv_full[1], 0)
+        mma_q.extend([("S", 0), ("commit", s_full[0]), ("commit", kv_empty[0]),
+                      ("commit", kv_empty[1])])
+        yield True
+        for j in range(nblk):
+            if j + 1 < nblk:
+                yield from wait(kv_full[0], j + 1)
+                yield from wait(kv_full[1], j + 1)
+                mma_q.extend([("S", j + 1), ("commit", s_full[(j + 1) & 1]),
+                              ("commit", kv_empty[0]), ("commit", kv_empty[1])])
+                yield True
+            yield from wait(p_full, j)
+            yield from wait(kv_full[2], j)
+            yield from wait(kv_full[3], j)
+            mma_q.extend([("PV", j), ("commit", pv_done), ("commit", kv_empty[2]),
+                          ("commit", kv_empty[3])])
+            yield True
+
+    def softmax(w):
+        for j in range(nblk):
+            b = j & 1
+            yield from wait(s_full[b], j >> 1)
+            if sbuf[b][w] != ("S", j):
+                raise Fail(f"warp {w} reads {sbuf[b][w]}, want S_{j}")
+            yield True
+            sbuf[b][w] = ("P", j)
+            yield True
+            if j > 0 and wait_pv:
+                yield from wait(pv_done, j - 1)
+            if j > 0 and rng.random() < p_rescale and o_last[0] != j - 1:
+                raise Fail(f"O rescaled at {j} while PV_{j - 1} may still write it")
+            if j > 0 and o_last[0] != j - 1:
+                raise Fail(f"r(P_{j}) written while PV_{j - 1} may still read r(P)")
+            pl[w] = j
+            yield True
+            p_full.arrive()
+            yield True
+        yield from wait(pv_done, nblk - 1)
+        if o_last[0] != nblk - 1:
+            raise Fail(f"epilogue reads O after PV_{o_last[0]}")
+
+    def pipe_step():
+        if not mma_q:
+            return False
+        op, a = mma_q.pop(0)
+        if op == "commit":
+            a.arrive()
+            return True
+        j = a
+        if op == "S":
+            if not q_in[0] or slot_tag[0] != j or slot_tag[1] != j:
+                raise Fail(f"S_{j} reads Q {q_in[0]} / K slots {slot_tag[:2]}")
+            slot_busy[0] = slot_busy[1] = False
+            b = j & 1
+            for w in range(4):
+                cur = sbuf[b][w]
+                if cur is not None and (cur[0] == "S" or o_last[0] is None or o_last[0] < cur[1]):
+                    raise Fail(f"S_{j} overwrites {cur} before it was consumed")
+                sbuf[b][w] = ("S", j)
+            return True
+        b = j & 1
+        for w in range(4):
+            if sbuf[b][w] != ("P", j) or pl[w] != j:
+                raise Fail(f"PV_{j} reads P {sbuf[b][w]} / r(P) {pl[w]}")
+        if slot_tag[2] != j or slot_tag[3] != j:
+            raise Fail(f"PV_{j} reads V slots {slot_tag[2:]}")
+        slot_busy[2] = slot_busy[3] = False
+        o_last[0] = j
+        return True
+
+    def tma_step():
+        if not tma_q:
+            return False
+        kind, j, s_, bar = tma_q.pop(rng.randrange(len(tma_q)))
+        if kind == "Q":
+            q_in[0] = True
+        else:
+            if slot_busy[s_]:
+                raise Fail(f"block {j} overwrites slot {s_} (block {slot_tag[s_]}) in use")
+            slot_tag[s_], slot_busy[s_] = j, True
+        bar.arrive()
+        return True
+
+    live = {"prod": producer(), "mma": mma()}
+    for w in range(4):
+        live[f"sm{w}"] = softmax(w)
+    _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q)
+
+
 def _schedule(rng, live, pipe_step, tma_step, mma_q, tma_q):
     """Runs the roles under a random scheduler with random stalls until all
     are done; raises Fail on a deadlock."""
@@ -964,3 +1087,15 @@ def test_model_finds_ring_overrun():
     with pytest.raises(Fail):
         for cfg in _configs_pair():
             run_pair(*cfg, odd_waits_its_slots=False)
+
+
+def test_exact_tc_protocol():
+    for seed in range(10):
+        for nblk in (1, 2, 3, 4, 7):
+            run_exact_tc(seed * 100 + nblk, nblk, (0.0, 0.5, 1.0)[seed % 3])
+
+
+def test_model_finds_r_of_p_overwrite():
+    with pytest.raises(Fail):
+        for seed in range(40):
+            run_exact_tc(seed, 5, 0.0, wait_pv=False)
