@@ -200,9 +200,9 @@ int llmr_mrope(llmr_ctx *ctx, float *data, const float *cos_t,
  * signature compatibility and ignored (may be NULL): no S x S buffer is
  * materialised. head_dim 64 or 128. head_dim 64 runs on the tensor cores
  * (three TF32 products per fp32 product, fp32 accumulation) when the
- * context workspace holds 4*n_heads*64*(2*seq_len + 2*ceil4(seq_len)) bytes
- * (llmr_ctx_reserve; ceil4 rounds up to a multiple of 4) for the operands'
- * TF32 residuals and V transposed; otherwise, and for head_dim 128, on an
+ * context workspace holds 4*n_heads*64*(4*seq_len + 2*ceil4(seq_len)) bytes
+ * (llmr_ctx_reserve; ceil4 rounds up to a multiple of 4) for the operands
+ * split into TF32 parts (V transposed); otherwise, and for head_dim 128, on an
  * fp32 FMA kernel. Both stay within 1e-5 of the reference's arithmetic. */
 int llmr_spatial_attention(llmr_ctx *ctx, const float *q, const float *k,
                            const float *v, float *scores, float *o,

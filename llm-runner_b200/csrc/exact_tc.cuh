@@ -2,25 +2,25 @@
 // lib/shaders/diffusion.slang:478-569: fp32 operands, fp32 dot products,
 // exact softmax) on the 5th-generation tensor cores, D = 64.
 //
-// Three-pass TF32 ("3xTF32"): tcgen05.mma kind::tf32 reads each fp32 operand
-// truncated to TF32 (the 13 low mantissa bits dropped). Writing x = t(x) +
-// r(x) with r(x) = x - t(x) (exact in fp32), each product is
-//   a*b ~= t(a) t(b) + t(a) t(r(b)) + t(r(a)) t(b)
-// with a relative error near 2^-20 (the dropped r*r term and the truncation
-// of r), accumulated in fp32 in TMEM. The raw fp32 tensors serve as t(x)
-// directly (the MMA truncates them); r(x) comes from a small kernel
-// (tf32_prepare_kernel, which also transposes V: kind::tf32 takes no
-// MN-major shared-memory operand) and from the softmax threads for P.
+// Three-pass TF32 ("3xTF32"): tcgen05.mma kind::tf32 reads fp32 operands as
+// TF32 (the 13 low mantissa bits dropped). Each operand is split as
+// x = g(x) + r(x), g(x) = x rounded to the nearest TF32 value, r(x) = x - g(x)
+// (exact in fp32, |r| <= 2^-11 |x|), and each product as
+//   a*b ~= g(a) g(b) + g(a) r(b) + r(a) g(b)
+// whose error (the dropped r*r term and the truncation of r to TF32) is
+// below 2^-20 relative, accumulated in fp32 in TMEM. A small kernel
+// (tf32_prepare_kernel) writes g and r of Q and K, and of V transposed
+// (kind::tf32 takes no MN-major shared-memory operand); the softmax threads
+// split P themselves.
 //
 // CTA = 128 query rows of one (b, h); 192 threads:
 //   warps 0-3  softmax (thread i owns query row i = TMEM lane i)
-//   warp  4    TMA producer: Q and r(Q) once, then per 128-key block
-//              K, r(K), V^T, r(V)^T into four 32 KB slots
+//   warp  4    TMA producer: g(Q) and r(Q) once, then per 128-key block
+//              g(K), r(K), g(V)^T, r(V)^T into four 32 KB slots
 //   warp  5    TMEM owner and MMA issuer (one elected lane)
 // TMEM (512 columns): S0 [0,128) S1 [128,256) r(P) [256,384) O [384,448).
 // S_j lands in buffer j&1 while the softmax works on the other one; the
-// softmax writes P_j (fp32, as t(P)) over S_j and r(P_j) into its own
-// columns; MMA order: S_0, then per block S_{j+1}, PV_j. P feeds the MMA
+// softmax writes g(P_j) over S_j and r(P_j) into its own columns; MMA order: S_0, then per block S_{j+1}, PV_j. P feeds the MMA
 // from TMEM. The row max is lazy (P rescaled only when the max grows by more
 // than 2^8), which is exact softmax up to fp32 rounding.
 #pragma once
@@ -60,21 +60,24 @@ __host__ __device__ constexpr uint32_t idesc_tf32(uint32_t M, uint32_t N, uint32
          ((M >> 4) << 24);
 }
 
-// x minus x truncated to TF32: the part the tensor core drops. Exact in fp32.
-__device__ __forceinline__ float tf32_residual(float x) {
-  return x - __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+// x rounded to the nearest TF32 value (ties away from zero): the "big" part
+// of the split; its 13 low mantissa bits are zero, so the tensor core reads
+// it exactly.
+__device__ __forceinline__ float tf32_big(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
 }
 
 // Operand preparation for the tensor-core exact kernel, dense fp32
-// [B*H][S][D] inputs: qr, kr = TF32 residuals of Q and K (same layout);
-// vt, vtr = V and its residual transposed to [B*H][D][Sp] (keys contiguous,
-// Sp = S rounded up to a multiple of 4 so rows are 16-byte aligned). The
-// P.V product needs V as a K-major operand: kind::tf32 takes no MN-major
-// (transposed) shared-memory operand. Grid (ceil(S/32), D/32, B*H), 32 x 8
-// threads: one 32 x 32 tile each, transposed through shared memory.
+// [B*H][S][D] inputs: g (big) and r (residual) parts of Q and K in the same
+// layout, and of V transposed to [B*H][D][Sp] (keys contiguous, Sp = S
+// rounded up to a multiple of 4 so rows are 16-byte aligned). Grid
+// (ceil(S/32), D/32, B*H), 256 threads: one 32 x 32 tile each, V transposed
+// through shared memory.
 __global__ void __launch_bounds__(256)
-    tf32_prepare_kernel(const float *q, const float *k, const float *v, float *qr, float *kr,
-                        float *vt, float *vtr, int S, int Sp, int D) {
+    tf32_prepare_kernel(const float *q, const float *k, const float *v, float *qg, float *qr,
+                        float *kg, float *kr, float *vtg, float *vtr, int S, int Sp, int D) {
   __shared__ float tile[32][33];
   const long long bh = blockIdx.z;
   const int s0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
@@ -84,8 +87,12 @@ __global__ void __launch_bounds__(256)
     const int s = s0 + r;
     if (s < S) {
       const long long i = base + (long long)s * D + d0 + tx;
-      qr[i] = tf32_residual(q[i]);
-      kr[i] = tf32_residual(k[i]);
+      const float xq = q[i], xk = k[i];
+      const float gq = tf32_big(xq), gk = tf32_big(xk);
+      qg[i] = gq;
+      qr[i] = xq - gq;
+      kg[i] = gk;
+      kr[i] = xk - gk;
       tile[r][tx] = v[i];
     }
   }
@@ -95,9 +102,10 @@ __global__ void __launch_bounds__(256)
     const int s = s0 + tx;
     if (s < S) {
       const float x = tile[tx][r];
+      const float g = tf32_big(x);
       const long long o = tbase + (long long)(d0 + r) * Sp + s;
-      vt[o] = x;
-      vtr[o] = tf32_residual(x);
+      vtg[o] = g;
+      vtr[o] = x - g;
     }
   }
 }
@@ -108,8 +116,8 @@ struct ExactTcCfg {
   static constexpr int BN = 128;                   // keys per block
   static constexpr int CHUNK = 128 * 128;          // 32 fp32 columns x 128 rows, SW128
   static constexpr int TILE = BM * D * 4;          // one fp32 tile of 128 rows (32 KB)
-  static constexpr int Q_OFF = 0;                  // Q, r(Q)
-  static constexpr int KV_OFF = 2 * TILE;          // slots: K, r(K), V^T, r(V)^T
+  static constexpr int Q_OFF = 0;                  // g(Q), r(Q)
+  static constexpr int KV_OFF = 2 * TILE;          // slots: g(K), r(K), g(V)^T, r(V)^T
   static constexpr int VCHUNK = 64 * 128;          // 32 keys x 64 d-rows of V^T, SW128
   static constexpr int BAR_OFF = KV_OFF + 4 * TILE;
   // barriers: q_full, kv_full[4], kv_empty[4], s_full[2], p_full, pv_done,
@@ -126,9 +134,9 @@ struct ExactTcCfg {
 // Lazy-max threshold (log2 units): P <= 2^8 between rescales.
 constexpr float kExactMaxExp = 8.0f;
 
-// Maps (fp32, SW128): tmQ/tmK and their residuals tmQr/tmKr over (d, s, h, b)
-// with 32 x 128 boxes; tmV/tmVr over V^T and its residual, (s, d, h, b) with
-// 32 x 64 boxes.
+// Maps (fp32, SW128): tmQ/tmK (g parts) and tmQr/tmKr (r parts) over
+// (d, s, h, b) with 32 x 128 boxes; tmV/tmVr over g(V)^T and r(V)^T,
+// (s, d, h, b) with 32 x 64 boxes.
 __global__ void __launch_bounds__(192, 1)
     attn_exact_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                          const __grid_constant__ CUtensorMap tmK,
@@ -146,7 +154,7 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *sKV = smem + C::KV_OFF;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
   uint64_t *q_full = bars;
-  uint64_t *kv_full = bars + 1;     // [slot]: 0 K, 1 r(K), 2 V^T, 3 r(V)^T
+  uint64_t *kv_full = bars + 1;     // [slot]: 0 g(K), 1 r(K), 2 g(V)^T, 3 r(V)^T
   uint64_t *kv_empty = kv_full + 4;
   uint64_t *s_full = kv_empty + 4;  // [buffer]
   uint64_t *p_full = s_full + 2;
@@ -226,7 +234,7 @@ __global__ void __launch_bounds__(192, 1)
     constexpr uint32_t IDESC_S = idesc_tf32(128, C::BN, 0);
     constexpr uint32_t IDESC_O = idesc_tf32(128, D, 0);  // V^T: K-major
     const uint32_t sQa = smem_u32(sQ), sKVa = smem_u32(sKV);
-    // S_buf = Q K^T + Q r(K)^T + r(Q) K^T over D (8 steps of K = 8 each).
+    // S_buf = g(Q) g(K)^T + g(Q) r(K)^T + r(Q) g(K)^T over D (8 steps of 8).
     auto issue_s = [&](int buf) {
 #pragma unroll
       for (int pass = 0; pass < 3; pass++) {
@@ -241,8 +249,8 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     };
-    // O (+)= P V + P r(V) + r(P) V over the block's 128 keys (16 steps of 8);
-    // V^T is the K-major B operand (rows d, keys contiguous).
+    // O (+)= g(P) g(V) + g(P) r(V) + r(P) g(V) over the block's 128 keys
+    // (16 steps of 8); V^T is the K-major B operand (rows d, keys contiguous).
     auto issue_pv = [&](int buf, bool acc) {
 #pragma unroll
       for (int pass = 0; pass < 3; pass++) {
@@ -320,16 +328,6 @@ __global__ void __launch_bounds__(192, 1)
       }
       const bool need = mx > m_used + kExactMaxExp;  // always on block 0
       const float m_tgt = need ? mx : m_used;
-      // P_j over S_j's own columns (already read; S_{j+2} comes after PV_j).
-      float ps = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 128; i++) {
-        const float pv = ex2_approx(__uint_as_float(sv[i]) - m_tgt);
-        ps += pv;
-        sv[i] = __float_as_uint(pv);
-      }
-#pragma unroll
-      for (int c = 0; c < 4; c++) tmem_st32(tS + c * 32, sv + c * 32);
       // PV_{j-1} has read r(P_{j-1}) and no longer accumulates into O.
       if (j > 0) {
         ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (j - 1) & 1, abort_flag));
@@ -351,13 +349,21 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       m_used = m_tgt;
-      l += ps;
+      // P_j in chunks of 32 keys: g(P) over S_j's own columns (already read;
+      // S_{j+2} comes after PV_j), r(P) into the r(P) columns.
 #pragma unroll
       for (int c = 0; c < 4; c++) {
-        uint32_t pl[32];
+        uint32_t pg[32], pr[32];
 #pragma unroll
-        for (int i = 0; i < 32; i++) pl[i] = __float_as_uint(tf32_residual(__uint_as_float(sv[c * 32 + i])));
-        tmem_st32(tmem + lane_off + C::PL_COL + c * 32, pl);
+        for (int i = 0; i < 32; i++) {
+          const float pv = ex2_approx(__uint_as_float(sv[c * 32 + i]) - m_tgt);
+          const float g = tf32_big(pv);
+          l += pv;
+          pg[i] = __float_as_uint(g);
+          pr[i] = __float_as_uint(pv - g);
+        }
+        tmem_st32(tS + c * 32, pg);
+        tmem_st32(tmem + lane_off + C::PL_COL + c * 32, pr);
       }
       tmem_wait_st();
       tc_fence_before();

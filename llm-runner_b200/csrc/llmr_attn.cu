@@ -374,11 +374,11 @@ bool exact_simt_forced() {
 }
 
 // Workspace floats the tensor-core exact kernel needs besides its inputs:
-// TF32 residuals of Q and K, and V^T with its residual (keys padded to a
-// multiple of 4 per row).
+// the TF32 big and residual parts of Q and K, and of V transposed (keys
+// padded to a multiple of 4 per row).
 long long exact_tc_extra_floats(long long B, long long H, long long S, long long D) {
   const long long Sp = (S + 3) / 4 * 4;
-  return 2 * B * H * S * D + 2 * B * H * D * Sp;
+  return 4 * B * H * S * D + 2 * B * H * D * Sp;
 }
 
 // Exact attention on the tensor cores (D = 64): q, k, v dense fp32
@@ -389,19 +389,20 @@ int launch_exact_tc(llmr_ctx *ctx, const float *q, const float *k, const float *
   const int D = C::D, B = ep.B, H = ep.H, S = ep.S;
   const int Sp = (S + 3) / 4 * 4;
   const long long n = (long long)B * H * S * D, nt = (long long)B * H * D * Sp;
-  float *qr = extra, *kr = extra + n, *vt = extra + 2 * n, *vtr = vt + nt;
+  float *qg = extra, *qr = extra + n, *kg = extra + 2 * n, *kr = extra + 3 * n;
+  float *vtg = extra + 4 * n, *vtr = vtg + nt;
   dim3 pgrid((S + 31) / 32, D / 32, B * H);
-  tf32_prepare_kernel<<<pgrid, 256, 0, ctx->stream>>>(q, k, v, qr, kr, vt, vtr, S, Sp, D);
+  tf32_prepare_kernel<<<pgrid, 256, 0, ctx->stream>>>(q, k, v, qg, qr, kg, kr, vtg, vtr, S, Sp, D);
   int rc = after_launch(ctx, "tf32_prepare");
   if (rc) return rc;
   const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
   const long long trs = Sp, ths = (long long)D * Sp, tbs = (long long)H * D * Sp;
   CUtensorMap mq, mk, mv, mqr, mkr, mvr;
-  if ((rc = make_map_f32(ctx, &mq, q, D, S, H, B, rs, hs, bs))) return rc;
-  if ((rc = make_map_f32(ctx, &mk, k, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mq, qg, D, S, H, B, rs, hs, bs))) return rc;
+  if ((rc = make_map_f32(ctx, &mk, kg, D, S, H, B, rs, hs, bs))) return rc;
   if ((rc = make_map_f32(ctx, &mqr, qr, D, S, H, B, rs, hs, bs))) return rc;
   if ((rc = make_map_f32(ctx, &mkr, kr, D, S, H, B, rs, hs, bs))) return rc;
-  if ((rc = make_map_f32(ctx, &mv, vt, S, D, H, B, trs, ths, tbs, 64))) return rc;
+  if ((rc = make_map_f32(ctx, &mv, vtg, S, D, H, B, trs, ths, tbs, 64))) return rc;
   if ((rc = make_map_f32(ctx, &mvr, vtr, S, D, H, B, trs, ths, tbs, 64))) return rc;
   CUDA_TRY(ctx, set_smem_once(attn_exact_tc_kernel, C::SMEM_BYTES));
   dim3 grid((S + C::BM - 1) / C::BM, B * H);

@@ -90,9 +90,9 @@ def test_workspace_sizes():
     assert L.workspace_bytes(L.make_desc(raw, 1, 1370, L.F16, L.F16)) == 0
     ex = L.AttnConfig(n_heads=4, head_dim=64, scale=0.125, exact=True)
     # fp32 Q, K, V and, for the tensor-core path (D = 64), their TF32 residuals
-    assert L.workspace_bytes(L.make_desc(ex, 1, 256, L.F32, L.F32)) == 7 * 4 * 256 * 64 * 4
+    assert L.workspace_bytes(L.make_desc(ex, 1, 256, L.F32, L.F32)) == 9 * 4 * 256 * 64 * 4
     assert L.workspace_bytes(L.make_desc(ex, 1, 1370, L.F32, L.F32)) == \
-        (5 * 4 * 1370 * 64 + 2 * 4 * 64 * 1372) * 4
+        (7 * 4 * 1370 * 64 + 2 * 4 * 64 * 1372) * 4
     ex128 = L.AttnConfig(n_heads=4, head_dim=128, scale=0.088, exact=True)
     assert L.workspace_bytes(L.make_desc(ex128, 1, 256, L.F32, L.F32)) == 3 * 4 * 256 * 128 * 4
     vae = L.AttnConfig(n_heads=1, head_dim=512, scale=512 ** -0.5)

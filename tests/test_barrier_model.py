@@ -868,9 +868,9 @@ def run_qkv_pair(seed, NST, k_blocks, tiles, p_stall=0.0, wait_acc_empty=True):
 def run_exact_tc(seed, nblk, p_rescale, wait_pv=True):
     """attn_exact_tc_kernel (exact_tc.cuh): one query tile; per block j the
     slots 0-3 hold K, r(K), V, r(V) of block j; S_j lands in TMEM buffer j&1
-    (MMA order S_0, then per block S_{j+1}, PV_j); the softmax writes P_j over
-    S_j at once, then waits for PV_{j-1} before it may rescale O and write
-    r(P_j) into the one r(P) buffer. wait_pv=False plants a bug: r(P_j)
+    (MMA order S_0, then per block S_{j+1}, PV_j); the softmax reads S_j, waits
+    for PV_{j-1}, may rescale O, then writes g(P_j) over S_j and r(P_j) into
+    the one r(P) buffer. wait_pv=False plants a bug: r(P_j)
     written (and O rescaled) without waiting for PV_{j-1}."""
     rng = random.Random(seed)
     q_full = Bar("q_full", 1)
@@ -923,10 +923,10 @@ def run_exact_tc(seed, nblk, p_rescale, wait_pv=True):
             if sbuf[b][w] != ("S", j):
                 raise Fail(f"warp {w} reads {sbuf[b][w]}, want S_{j}")
             yield True
-            sbuf[b][w] = ("P", j)
-            yield True
             if j > 0 and wait_pv:
                 yield from wait(pv_done, j - 1)
+            sbuf[b][w] = ("P", j)
+            yield True
             if j > 0 and rng.random() < p_rescale and o_last[0] != j - 1:
                 raise Fail(f"O rescaled at {j} while PV_{j - 1} may still write it")
             if j > 0 and o_last[0] != j - 1:

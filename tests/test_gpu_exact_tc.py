@@ -96,7 +96,7 @@ def test_spatial_attention_mirror_tensor_cores(ctx):
     rng = np.random.default_rng(11)
     q, k, v = (rng.standard_normal((H, S, D), dtype=np.float32) for _ in range(3))
     o = torch.full((H, S, D), float("nan"), device="cuda")
-    ctx.reserve(4 * H * D * (2 * S + 2 * ((S + 3) // 4 * 4)))
+    ctx.reserve(4 * H * D * (4 * S + 2 * ((S + 3) // 4 * 4)))
     n0 = ctx.launches
     L.spatial_attention(ctx, *(torch.from_numpy(a).cuda() for a in (q, k, v)), None, o, D, H, S,
                         0.125)
