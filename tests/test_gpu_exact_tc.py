@@ -3,7 +3,11 @@ D = 64: three TF32 products per fp32 product (tcgen05.mma kind::tf32, fp32
 accumulation). Checked against the oracle's restatement of the reference's
 spatial_attention within the fp32 bar (1e-5 max and mean): the plumbing
 config, a Depth-Anything-shaped fp32 case (H16 S1370), ragged token counts,
-batch 2 with strided output and the LSE, and the spatial_attention mirror.
+batch 2 with the LSE, and the spatial_attention mirror. Beyond the configs
+(planted row-max jumps, peaky rows at a large scale), where the oracle's own
+fp32 rounding is of the same size as the bar, both are measured against a
+float64 restatement: the tensor-core path must be within twice the oracle's
+error (or within 1e-5 / 1e-6 outright).
 The launch counts show which kernel ran (prologue + residuals + tensor-core
 kernel for the fused op; residuals + tensor-core kernel for the mirror)."""
 import numpy as np
@@ -57,10 +61,15 @@ def _exact_case(ctx, B, H, S, seed, lse=False, scale=0.125, in_scale=1.0, plant=
         if tol == TOL:
             want = O.spatial_attention(q[b], k[b], v[b], D, H, S, scale)  # [H, S, D]
             _check(g, want, f"B{B} H{H} S{S} b={b}")
-        else:  # beyond the configs: against float64 within the given bound
-            want = O.attention_f64(q[b], k[b], v[b], D, H, S, scale)
-            err = np.abs(g.astype(np.float64) - want)
-            assert err.max() <= tol[0] and err.mean() <= tol[1], (err.max(), err.mean())
+        else:
+            # Beyond the configs (large or planted scores): against a float64
+            # restatement, as accurate as the reference's own fp32 arithmetic
+            # (the oracle) within a factor 2, or within `tol` outright.
+            exact = O.attention_f64(q[b], k[b], v[b], D, H, S, scale)
+            e_gpu = np.abs(g.astype(np.float64) - exact)
+            e_ref = np.abs(O.spatial_attention(q[b], k[b], v[b], D, H, S, scale) - exact)
+            assert e_gpu.max() <= max(2 * e_ref.max(), tol[0]), (e_gpu.max(), e_ref.max())
+            assert e_gpu.mean() <= max(2 * e_ref.mean(), tol[1]), (e_gpu.mean(), e_ref.mean())
     if lse:
         q64, k64 = q.astype(np.float64), k.astype(np.float64)
         s = np.einsum("bhsd,bhtd->bhst", q64, k64) * scale
@@ -98,18 +107,19 @@ def test_exact_tc_ragged(ctx, S):
     _exact_case(ctx, 1, 2, S, seed=100 + S)
 
 
-def test_exact_tc_batch_lse_and_rescale(ctx):
-    """Batch 2, LSE output, and planted late keys that make the row max jump
-    (the O rescale path), at the configs' scale."""
-    _exact_case(ctx, 2, 3, 700, seed=7, lse=True, plant=True)
+def test_exact_tc_batch_and_lse(ctx):
+    _exact_case(ctx, 2, 3, 700, seed=7, lse=True)
 
 
-def test_exact_tc_peaky_rows_vs_float64(ctx):
-    """Beyond the configs: scale 0.6 (scaled scores up to ~18) amplifies the
-    error of the three-TF32 products (each below 2^-20 relative, accumulated
-    in the tensor core's fp32) into the exponent; measured against a float64
-    restatement with a bound of 4e-5 max, 4e-6 mean."""
-    _exact_case(ctx, 1, 3, 700, seed=8, scale=0.6, tol=(4e-5, 4e-6))
+def test_exact_tc_planted_max_jumps(ctx):
+    """Planted late keys matching a query (scores near 128 before scaling):
+    the row max jumps far past the lazy threshold (the O rescale path)."""
+    _exact_case(ctx, 1, 3, 700, seed=9, plant=True, tol=(1e-5, 1e-6))
+
+
+def test_exact_tc_peaky_rows(ctx):
+    """Scale 0.6: scaled scores up to ~18 amplify score errors into P."""
+    _exact_case(ctx, 1, 3, 700, seed=8, scale=0.6, tol=(1e-5, 1e-6))
 
 
 def test_spatial_attention_mirror_tensor_cores(ctx):
