@@ -635,6 +635,66 @@ def f64_rows(q, k, v, qg, kg, cos, sin, case, rows, heads):
     return torch.cat(out, dim=1)
 
 
+def roofline_block(case, achieved, peak, peak_kind, traffic):
+    """Roofline of the dominant kernel. The fp16/bf16 configs run on
+    kind::f16 (bound: the measured dense BF16 peak). The fp32 exact config
+    runs three TF32 products per fp32 product on kind::tf32, whose rate is
+    half the BF16 rate: its tensor-pipe bound for algorithmic flops is a
+    sixth of the BF16 peak."""
+    if case.exact and case.head_dim == 64:
+        bound = peak / 6.0
+        return {"bound": "tensor", "achieved": achieved, "peak": bound, "unit": "TFLOP/s",
+                "frac": achieved / bound, "traffic": None,
+                "kernel": "attn_exact_tc_kernel (3xTF32, kind::tf32)",
+                "peak_source": f"{peak_kind} bf16_tflops / 2 (TF32 rate) / 3 (passes)",
+                "note": "achieved includes the TF32 split kernel (the op's second phase)"}
+    return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+            "frac": achieved / peak, "traffic": traffic,
+            "kernel": f"fa_fwd_tc_kernel<{case.head_dim}, {case.dtype}>",
+            "peak_source": f"{peak_kind} bf16_tflops (burst)"}
+
+
+def exact_depth_block(args, local, peak, peak_kind):
+    """The exact fp32 path on a Depth-Anything-shaped case (B1 H16 S1370 D64,
+    0.5 * N(0, 1), scale 1/8) through the spatial_attention mirror: the
+    tensor-core kernel (context workspace reserved) against the fp32 FMA
+    kernel (no workspace), CUDA events, L2 flushed between steps."""
+    import numpy as np
+    import torch
+
+    import llmr_attn as L
+    H, S, D = 16, 1370, 64
+    rng = np.random.default_rng(1)
+    q, k, v = (torch.from_numpy(rng.standard_normal((H, S, D), dtype=np.float32) * 0.5)
+               .to(f"cuda:{local}") for _ in range(3))
+    o = torch.empty((H, S, D), device=f"cuda:{local}")
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=f"cuda:{local}")
+    flops = 4.0 * H * S * S * D
+    res = {"workload": f"spatial_attention mirror, H{H} S{S} D{D} fp32 [H, S, D]"}
+    for name, ws in (("tensor_cores", 4 * H * D * (4 * S + 2 * ((S + 3) // 4 * 4))),
+                     ("fma", 0)):
+        ctx = L.Context(local, workspace_bytes=ws)
+        call = lambda: L.spatial_attention(ctx, q, k, v, None, o, D, H, S, 0.125)
+        for _ in range(3):
+            call()
+        ctx.sync()
+        ts = []
+        for _ in range(max(5, min(args.steps, 20))):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            call()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        ms = sum(ts) / len(ts)
+        res[name] = {"ms": ms, "tflops": flops / (ms / 1e3) / 1e12}
+        ctx.close()
+    res["tensor_core_frac_of_bound"] = res["tensor_cores"]["tflops"] / (peak / 6.0)
+    res["speedup_over_fma"] = res["fma"]["ms"] / res["tensor_cores"]["ms"]
+    return res
+
+
 def strong_scaling_block(args, world, rank, local):
     """The north star's multi-GPU target, measured inside the same torchrun
     launch as the weak-scaling line: Qwen-Image-Edit 2048^2 (B1 H24 S33792
@@ -1075,8 +1135,9 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-        "data": "synthetic (seeded N(0,1) bf16 Q/K/V, U(0.8,1.2) gains)",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": case.dtype,
+        "data": f"synthetic (seeded N(0,1) {case.dtype} Q/K/V"
+                + (f", {case.gain} gains)" if case.norm else ")"),
         "config": config_block(case, world),
         "value_per_gpu": value / world,
         "pct_of_peak": 100.0 * (value / world) / peak,
@@ -1084,10 +1145,7 @@ def main():
                       "note": "each kernel timed alone (library events between the launches); "
                               "ms_per_step overlaps the attention kernel's set-up with the "
                               "prologue's tail (programmatic dependent launch)"},
-        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
-                     "unit": "TFLOP/s", "frac": achieved / peak, "traffic": traffic,
-                     "kernel": "fa_fwd_tc_kernel<128, bf16>",
-                     "peak_source": f"{peak_kind} bf16_tflops (burst)"},
+        "roofline": roofline_block(case, achieved, peak, peak_kind, traffic),
         "e2e": {"value": world * flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
                 "h2d_bytes_per_step": 3 * dc.q.numel() * dc.q.element_size(),
                 "d2h_bytes_per_step": dc.o.numel() * dc.o.element_size(),
@@ -1098,6 +1156,8 @@ def main():
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if case.exact:
+        line["exact_depth_shaped"] = exact_depth_block(args, local, peak, peak_kind)
     if world > 1 and not args.no_strong:
         line["strong_scaling"] = strong_scaling_block(args, world, rank, local)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
