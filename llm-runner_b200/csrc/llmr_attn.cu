@@ -334,12 +334,9 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
             (st == nullptr || (st[0] % VIN == 0 && st[1] % VIN == 0 && st[2] % VIN == 0)));
   };
   const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs) && ok(pp.cos_t, nullptr) &&
-                   ok(pp.sin_t, nullptr) && ok(pp.q_gain, nullptr) && ok(pp.k_gain, nullptr);
-  if (vec) {
-    CUDA_TRY(ctx, set_smem_once(prologue_kernel<D, InT, OutT, true>, prologue_smem_bytes<D>()));
-    prologue_kernel<D, InT, OutT, true><<<blocks, 256, prologue_smem_bytes<D>(), ctx->stream>>>(
-        vq, vk, vv, out, pp);
-  }
+                   ok(pp.sin_t, nullptr);
+  if (vec)
+    prologue_kernel<D, InT, OutT, true><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   else
     prologue_kernel<D, InT, OutT, false><<<blocks, 256, 0, ctx->stream>>>(vq, vk, vv, out, pp);
   return after_launch(ctx, "prologue");

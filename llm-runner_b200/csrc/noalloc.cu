@@ -138,14 +138,9 @@ int prologue(cudaStream_t st, int num_sms, const void *q, const void *k, const v
                               (s == nullptr || (s[0] % VIN == 0 && s[1] % VIN == 0 && s[2] % VIN == 0)));
   };
   const bool vec = ok(q, qs) && ok(k, ks) && ok(v, vs) && ok(pp.cos_t, nullptr) &&
-                   ok(pp.sin_t, nullptr) && ok(pp.q_gain, nullptr) && ok(pp.k_gain, nullptr);
-  if (vec) {
-    if (set_smem_once(prologue_kernel<D, InT, __half, true>, prologue_smem_bytes<D>()) !=
-        cudaSuccess)
-      return LLMR_ECUDA;
-    prologue_kernel<D, InT, __half, true><<<blocks, 256, prologue_smem_bytes<D>(), st>>>(
-        vq, vk, vv, out, pp);
-  }
+                   ok(pp.sin_t, nullptr);
+  if (vec)
+    prologue_kernel<D, InT, __half, true><<<blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
   else
     prologue_kernel<D, InT, __half, false><<<blocks, 256, 0, st>>>(vq, vk, vv, out, pp);
   return cudaGetLastError() == cudaSuccess ? LLMR_OK : LLMR_ECUDA;

@@ -54,21 +54,6 @@ __device__ __forceinline__ void griddep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
-// 16-byte global -> shared copy that bypasses L1 and completes
-// asynchronously (commit / wait groups); src_bytes = 0 writes zeros.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-               "r"(src_bytes)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 // Prologue geometry: a row (one token of one head) is D elements, handled by
 // an 8-lane group with E = D/8 elements per lane, so a warp works on 4 rows
 // at once and the RMSNorm sum needs a 3-step shuffle. A CTA of 8 warps walks
@@ -78,15 +63,6 @@ constexpr int kProRowsPerWarpStep = 32 / kProLanesPerRow;  // 4
 constexpr int kProWarps = 8;
 constexpr int kProSteps = 4;  // row groups per warp
 constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 128
-
-// Shared memory of the vectorised prologue: the CTA's 128 table rows (cos,
-// then sin, D/2 floats each) and both gain sets, staged with cp.async while
-// the rows' data loads are in flight, so the per-row RoPE and gain reads hit
-// shared memory instead of waiting on L2 one row at a time.
-template <int D>
-constexpr int prologue_smem_bytes() {
-  return 2 * kProRowsPerCta * (D / 2) * 4 + 2 * D * 4;
-}
 
 // Grid (ceil(S / 128), B*H, 3): blockIdx.z selects Q, K or V, blockIdx.y the
 // (b, h) unit. Q and K rows get the per-head RMSNorm of batch_head_norm
@@ -124,33 +100,6 @@ __global__ void __launch_bounds__(256)
   const int row_in_warp = lane / kProLanesPerRow;
   const int s_base = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * kProRowsPerWarpStep +
                      row_in_warp;
-  // VEC: the CTA's table rows and gains go to shared memory (cp.async, in
-  // flight together with the data loads below).
-  extern __shared__ __align__(16) float pro_smem[];
-  float *s_cos = pro_smem;
-  float *s_sin = s_cos + kProRowsPerCta * (D / 2);
-  float *s_gain = s_sin + kProRowsPerCta * (D / 2);
-  if (VEC) {
-    const int s0 = blockIdx.x * kProRowsPerCta;
-    if (rope) {
-      constexpr int PER_ROW = D / 8;  // 16-byte pieces per table row
-      for (int i = threadIdx.x; i < kProRowsPerCta * PER_ROW; i += blockDim.x) {
-        const int r = i / PER_ROW, c = i - r * PER_ROW;
-        const bool rin = s0 + r < p.S;
-        const long long trow = (long long)p.rope_row_offset + (rin ? s0 + r : 0);
-        cp_async16(smem_u32(s_cos + r * (D / 2) + c * 4), p.cos_t + trow * (D / 2) + c * 4,
-                   rin ? 16u : 0u);
-        cp_async16(smem_u32(s_sin + r * (D / 2) + c * 4), p.sin_t + trow * (D / 2) + c * 4,
-                   rin ? 16u : 0u);
-      }
-    }
-    if (gain != nullptr) {
-      const int n = (p.split_row > 0 ? 2 : 1) * D / 4;
-      for (int i = threadIdx.x; i < n; i += blockDim.x)
-        cp_async16(smem_u32(s_gain + i * 4), gain + i * 4, 16u);
-    }
-    cp_async_commit();
-  }
   // All row groups' loads are issued before any is used, so a warp keeps
   // kProSteps * 16 * (E / VIN) bytes per lane in flight.
   Pack<InT, VIN> raw[kProSteps][E / VIN];
@@ -163,10 +112,6 @@ __global__ void __launch_bounds__(256)
       for (int c = 0; c < E / VIN; c++)
         raw[step][c] = *reinterpret_cast<const Pack<InT, VIN> *>(src + c * VIN);
     }
-  }
-  if (VEC) {
-    cp_async_wait<0>();
-    __syncthreads();
   }
 #pragma unroll
   for (int step = 0; step < kProSteps; step++) {
@@ -198,17 +143,13 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
       for (int o = kProLanesPerRow / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float rms = rsqrtf(ss / (float)D + p.eps);
-      const float *g = (VEC ? s_gain : gain) + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) +
-                       sub * E;
+      const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + sub * E;
 #pragma unroll
       for (int e = 0; e < E; e++) x[e] = __fmul_rn(__fmul_rn(x[e], rms), g[e]);
     }
     if (rope && in) {
-      const int srow = s - blockIdx.x * kProRowsPerCta;  // row within the staged tables
-      const float *ct = VEC ? s_cos + srow * (D / 2) + sub * (E / 2)
-                            : p.cos_t + grow * (D / 2) + sub * (E / 2);
-      const float *st = VEC ? s_sin + srow * (D / 2) + sub * (E / 2)
-                            : p.sin_t + grow * (D / 2) + sub * (E / 2);
+      const float *ct = p.cos_t + grow * (D / 2) + sub * (E / 2);
+      const float *st = p.sin_t + grow * (D / 2) + sub * (E / 2);
       float cv[E / 2], sv[E / 2];
       if (VEC) {
 #pragma unroll
@@ -244,6 +185,21 @@ __global__ void __launch_bounds__(256)
       }
     }
   }
+}
+
+// 16-byte global -> shared copy that bypasses L1 and completes
+// asynchronously (commit / wait groups); src_bytes = 0 writes zeros.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // The prologue arithmetic of prologue_kernel for one lane's slice of one row
