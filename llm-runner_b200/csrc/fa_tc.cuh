@@ -61,17 +61,28 @@ struct FaParams {
 // done, 2 + 2k / 3 + 2k producer begins unit k / its K'/V' are ready (k < 4),
 // 10 + 2k / 11 + 2k tile 0's first S of unit k ready / epilogue done,
 // 18 background Q' of unit 1 done, 19 background K'/V' pieces done,
-// 20 background done, 21 kernel end.
-constexpr int kTimelineSlots = 32;
+// 20 background done, 21 kernel end (all %globaltimer ns). Slots 32-63, SM
+// clock cycles (clock64) of the softmax of tile 0, row 0, in blocks 4-11 of
+// the CTA's second unit: 32 + 4i S_j ready, +1 row max done, +2 P keys 0-63
+// handed over, +3 P keys 64-127 handed over (i = j - 4).
+constexpr int kTimelineSlots = 64;
 #ifdef LLMR_TIMELINE
 #define LLMR_TL(slot)                                                                    \
   do {                                                                                   \
     if (p.timeline)                                                                      \
       p.timeline[(size_t)blockIdx.x * kTimelineSlots + (slot)] = globaltimer_ns();       \
   } while (0)
+#define LLMR_TLC(slot)                                                                   \
+  do {                                                                                   \
+    if (p.timeline)                                                                      \
+      p.timeline[(size_t)blockIdx.x * kTimelineSlots + (slot)] = clock64();              \
+  } while (0)
 #else
 #define LLMR_TL(slot) \
   do {                \
+  } while (0)
+#define LLMR_TLC(slot) \
+  do {                 \
   } while (0)
 #endif
 
@@ -167,7 +178,12 @@ struct FaCfg {
   // shared memory left over (the non-fused kernel leaves it unused).
   static constexpr int BG_OFF = (BAR_OFF + NBAR * 8 + 16 + 127) / 128 * 128;
   static constexpr int BG_RING = 12 * 1024;  // bytes per background warp
-  static constexpr int SMEM_BYTES = BG_OFF + 2 * BG_RING + 1024;  // +align slack
+  // Without the fused prologue the same region stages the epilogue's output
+  // rows: 4 KB per softmax warp (32 rows x 128 bytes).
+  static constexpr int EPI_OFF = BG_OFF;
+  static constexpr int EPI_BYTES = 8 * 4096;
+  static constexpr int REGION = EPI_BYTES > 2 * BG_RING ? EPI_BYTES : 2 * BG_RING;
+  static constexpr int SMEM_BYTES = BG_OFF + REGION + 1024;  // +align slack
   static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
   static constexpr int THREADS = 384;
   // Register split (setmaxnreg): the two softmax warpgroups hold a whole
@@ -694,6 +710,8 @@ __global__ void __launch_bounds__(384, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], jj & 1, abort_flag));
         if (!ok) break;
         if (j == 0 && k < 4 && threadIdx.x == 0) LLMR_TL(10 + 2 * k);
+        const bool tl_blk = k == 1 && j >= 4 && j < 12 && threadIdx.x == 0;
+        if (tl_blk) LLMR_TLC(32 + 4 * (j - 4));
         tc_fence_after();
         const int valid = un.sk - j * C::BN;  // keys of this block inside the sequence
         // Applies the key mask (keys past the sequence -> -inf) to chunk c.
@@ -725,6 +743,7 @@ __global__ void __launch_bounds__(384, 1)
         // block's row max passes it by more than kMaxExp (P would overflow
         // fp16), and on the first block; O and l are rescaled then.
         const float m_new = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sl2;
+        if (tl_blk) LLMR_TLC(33 + 4 * (j - 4));
         const bool need = m_new > m_used + kMaxExp;  // always true on block 0
         if (__any_sync(0xffffffffu, need)) {
           const float m_tgt = need ? m_new : m_used;
@@ -774,6 +793,7 @@ __global__ void __launch_bounds__(384, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_half[2 * t + (c >> 1)]);
+            if (tl_blk) LLMR_TLC(34 + (c >> 1) + 4 * (j - 4));
           }
         }
         const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
@@ -806,6 +826,60 @@ __global__ void __launch_bounds__(384, 1)
         ct = wt * inv / l;
         lse_out = mx2 + logf(wa + wt);
       }
+      if (!FUSED && !merge) {
+        // Coalesced stores through shared memory: each round, every lane puts
+        // 128 bytes of its row (64 columns of 16-bit output, 32 of fp32) into
+        // the warp's staging block (16-byte pieces XOR-swizzled by row), then
+        // the warp writes 4 whole 128-byte row segments per store instruction.
+        constexpr int CPR = 128 / (int)sizeof(OutT);  // columns per round
+        uint8_t *stg = smem + C::EPI_OFF + warp * 4096;
+        const int rbase = un.q0 + t * C::BM + (warp & 3) * 32;  // the warp's first row
+#pragma unroll
+        for (int rnd = 0; rnd < D / CPR; rnd++) {
+#pragma unroll
+          for (int cc = 0; cc < CPR / 32; cc++) {
+            const int c = rnd * (CPR / 32) + cc;
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+            reg_fence32(o);
+            if (c == D / 32 - 1) {
+              // O_t is read out: the next unit's first PV may overwrite it.
+              tc_fence_before();
+              __syncwarp();
+              if (lane == 0) mbar_arrive(&o_empty[t]);
+            }
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) v[i] = __uint_as_float(o[i]) * ct;
+            // 32 columns = 32 * sizeof(OutT) bytes = 2 or 8 pieces of 16 bytes
+            constexpr int PIECES = 32 * (int)sizeof(OutT) / 16;
+            alignas(16) OutT pk[32];
+#pragma unroll
+            for (int i = 0; i < 32; i++) pk[i] = from_f32<OutT>(v[i]);
+#pragma unroll
+            for (int pc = 0; pc < PIECES; pc++) {
+              const int piece = cc * PIECES + pc;
+              *reinterpret_cast<uint4 *>(stg + lane * 128 + ((piece ^ (lane & 7)) << 4)) =
+                  reinterpret_cast<const uint4 *>(pk)[pc];
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; it++) {
+            const int pid = it * 32 + lane, r = pid >> 3, part = pid & 7;
+            const uint4 val = *reinterpret_cast<const uint4 *>(stg + r * 128 + ((part ^ (r & 7)) << 4));
+            const int rloc = rbase + r;  // query within its sequence
+            if (rloc < un.sq) {
+              OutT *d = reinterpret_cast<OutT *>(p.o) + (long long)b * p.o_batch_stride +
+                        (long long)(un.row0 + rloc) * p.o_row_stride + (long long)h * D +
+                        rnd * CPR + part * (16 / (int)sizeof(OutT));
+              *reinterpret_cast<uint4 *>(d) = val;
+            }
+          }
+          __syncwarp();
+        }
+      } else {
 #pragma unroll
       for (int c = 0; c < D / 32; c++) {
         uint32_t o[32];
@@ -834,6 +908,7 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         if (qin) store_row_chunk<OutT>(dst + c * 32, v);
+      }
       }
       if (p.lse != nullptr && qin) p.lse[(long long)bh * S + qrow] = lse_out;
       if (k < 4 && threadIdx.x == 0) LLMR_TL(11 + 2 * k);

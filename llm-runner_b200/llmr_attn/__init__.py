@@ -212,7 +212,7 @@ class Context:
 
     def timeline(self, buf) -> None:
         """Diagnostic builds: per-CTA event timestamps of the attention kernel
-        into `buf` (a uint64/int64 CUDA tensor of >= num_sms * 32 elements;
+        into `buf` (a uint64/int64 CUDA tensor of >= num_sms * 64 elements;
         None turns it off)."""
         nbytes = 0 if buf is None else buf.numel() * buf.element_size()
         self.check(lib.llmr_timeline_set(self.handle, _ptr(buf), nbytes))
