@@ -80,10 +80,27 @@ def parse():
 
 def profile_run(args):
     """Exactly W + K fused calls of the configuration on cuda:0 and nothing
-    else, so that an ncu launch list or capture sees only the op's kernels."""
+    else, so that an ncu launch list or capture sees only the op's kernels.
+    --config depth_fp32: the spatial_attention mirror on the Depth-shaped fp32
+    case (H16 S1370 D64) on the tensor cores instead."""
     import torch
 
     import llmr_attn as L
+    if args.config == "depth_fp32":
+        import numpy as np
+        H, S, D = 16, 1370, 64
+        rng = np.random.default_rng(1)
+        q, k, v = (torch.from_numpy(rng.standard_normal((H, S, D), dtype=np.float32) * 0.5)
+                   .cuda() for _ in range(3))
+        o = torch.empty((H, S, D), device="cuda")
+        ctx = L.Context(0, workspace_bytes=4 * H * D * (4 * S + 2 * ((S + 3) // 4 * 4)))
+        for _ in range(args.warmup + args.steps):
+            L.spatial_attention(ctx, q, k, v, None, o, D, H, S, 0.125)
+        ctx.sync()
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_run": "depth_fp32 spatial_attention mirror",
+                          "calls": args.warmup + args.steps, "launches": ctx.launches}))
+        return
     from llmr_attn import configs as C
     from llmr_attn.runner import to_device
     case = C.CASES[args.config]

@@ -227,6 +227,11 @@ inline dim3 fa_grid(FaParams &p, int B, int num_sms) {
 #endif
 constexpr uint32_t kExp2EmuMask = LLMR_EXP2_EMU_MASK;
 
+#ifndef LLMR_HALF0_AT
+#define LLMR_HALF0_AT 1
+#endif
+constexpr int kHalf0At = LLMR_HALF0_AT;  // chunk after which P keys 0-63 are handed over
+
 // Largest exponent argument x = s*scale*log2e - m the softmax lets through
 // without rescaling: P = 2^x <= 2^15 stays finite in fp16 (max 65504) with
 // the same 2^-11 relative rounding as any other value, and O / l accumulate
@@ -788,12 +793,15 @@ __global__ void __launch_bounds__(384, 1)
             pk[i] = pack_f16x2(pf.x, pf.y);
           }
           tmem_st16(tS + c * 16, pk);
-          if (c == 1 || c == 3) {
+          // Keys 0-63 are handed over after chunk kHalf0At's stores (1: as
+          // soon as they are written; 2: one chunk later, so the warp does not
+          // stall on the store round trip in mid-row), keys 64-127 at the end.
+          if (c == kHalf0At || c == 3) {
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_half[2 * t + (c >> 1)]);
-            if (tl_blk) LLMR_TLC(34 + (c >> 1) + 4 * (j - 4));
+            if (lane == 0) mbar_arrive(&p_half[2 * t + (c == 3 ? 1 : 0)]);
+            if (tl_blk) LLMR_TLC(34 + (c == 3 ? 1 : 0) + 4 * (j - 4));
           }
         }
         const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);
