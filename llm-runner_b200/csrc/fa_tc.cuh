@@ -834,7 +834,9 @@ __global__ void __launch_bounds__(384, 1)
         ct = wt * inv / l;
         lse_out = mx2 + logf(wa + wt);
       }
-      if (!FUSED && !merge) {
+      // The choice must be warp-uniform (the staged path's TMEM loads and
+      // shuffles are warp-collective): it depends on the launch, not the row.
+      if (!FUSED && !(kCanMerge && p.merge)) {
         // Coalesced stores through shared memory: each round, every lane puts
         // 128 bytes of its row (64 columns of 16-bit output, 32 of fp32) into
         // the warp's staging block (16-byte pieces XOR-swizzled by row), then

@@ -73,8 +73,11 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 // dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
 // applies on load, or fp32 for the exact path). VEC: every lane's slice of
 // the inputs and tables is 16-byte aligned (checked on the host).
+#ifndef LLMR_PRO_MIN_CTAS
+#define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
+#endif
 template <int D, typename InT, typename OutT, bool VEC>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
     prologue_kernel(View<InT> q, View<InT> k, View<InT> v, OutT *out,
                     ProParams p) {
   constexpr int E = D / kProLanesPerRow;  // 16 (D=128) or 8 (D=64)
