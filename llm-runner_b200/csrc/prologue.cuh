@@ -73,9 +73,6 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 // dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
 // applies on load, or fp32 for the exact path). VEC: every lane's slice of
 // the inputs and tables is 16-byte aligned (checked on the host).
-#ifndef LLMR_PRO_HOIST
-#define LLMR_PRO_HOIST 0  // 1: load every row group's table slices with the data
-#endif
 #ifndef LLMR_PRO_MIN_CTAS
 #define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
 #endif
@@ -119,23 +116,6 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
         raw[step][c] = *reinterpret_cast<const Pack<InT, VIN> *>(src + c * VIN);
     }
   }
-#if LLMR_PRO_HOIST
-  // The RoPE table slices of every row group, loaded with the data so that
-  // their latency overlaps it instead of following each row's norm.
-  float4 tcs[kProSteps][E / 8], tsn[kProSteps][E / 8];
-  if (VEC && rope) {
-#pragma unroll
-    for (int step = 0; step < kProSteps; step++) {
-      const int s = s_base + step * kProRowsPerWarpStep * kProWarps;
-      const long long grow = (long long)p.rope_row_offset + (s < p.S ? s : 0);
-#pragma unroll
-      for (int c = 0; c < E / 8; c++) {
-        tcs[step][c] = __ldg(reinterpret_cast<const float4 *>(p.cos_t + grow * (D / 2) + sub * (E / 2)) + c);
-        tsn[step][c] = __ldg(reinterpret_cast<const float4 *>(p.sin_t + grow * (D / 2) + sub * (E / 2)) + c);
-      }
-    }
-  }
-#endif
 #pragma unroll
   for (int step = 0; step < kProSteps; step++) {
     const int s = s_base + step * kProRowsPerWarpStep * kProWarps;
@@ -174,17 +154,6 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
       const float *ct = p.cos_t + grow * (D / 2) + sub * (E / 2);
       const float *st = p.sin_t + grow * (D / 2) + sub * (E / 2);
       float cv[E / 2], sv[E / 2];
-#if LLMR_PRO_HOIST
-      if (VEC) {
-#pragma unroll
-        for (int c = 0; c < E / 8; c++) {
-          cv[4 * c] = tcs[step][c].x; cv[4 * c + 1] = tcs[step][c].y;
-          cv[4 * c + 2] = tcs[step][c].z; cv[4 * c + 3] = tcs[step][c].w;
-          sv[4 * c] = tsn[step][c].x; sv[4 * c + 1] = tsn[step][c].y;
-          sv[4 * c + 2] = tsn[step][c].z; sv[4 * c + 3] = tsn[step][c].w;
-        }
-      } else
-#else
       if (VEC) {
 #pragma unroll
         for (int c = 0; c < E / 2; c += 4) {
@@ -193,9 +162,7 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
           cv[c] = a.x; cv[c + 1] = a.y; cv[c + 2] = a.z; cv[c + 3] = a.w;
           sv[c] = bq.x; sv[c + 1] = bq.y; sv[c + 2] = bq.z; sv[c + 3] = bq.w;
         }
-      } else
-#endif
-      {
+      } else {
 #pragma unroll
         for (int e = 0; e < E / 2; e++) {
           cv[e] = ct[e];
