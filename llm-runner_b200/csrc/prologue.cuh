@@ -76,25 +76,17 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 #ifndef LLMR_PRO_MIN_CTAS
 #define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
 #endif
-#ifndef LLMR_PRO_LPR
-#define LLMR_PRO_LPR 8  // lanes per row in prologue_kernel (8 or 16)
-#endif
 template <int D, typename InT, typename OutT, bool VEC>
 __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
     prologue_kernel(View<InT> q, View<InT> k, View<InT> v, OutT *out,
                     ProParams p) {
-  // Local geometry: LPR lanes per row, RPW rows per warp step, STEPS steps
-  // per warp, 128 rows per CTA either way.
-  constexpr int LPR = (D / LLMR_PRO_LPR) >= 8 ? LLMR_PRO_LPR : D / 8;
-  constexpr int RPW = 32 / LPR;
-  constexpr int STEPS = kProRowsPerCta / (RPW * kProWarps);
-  constexpr int E = D / LPR;  // elements per lane
+  constexpr int E = D / kProLanesPerRow;  // 16 (D=128) or 8 (D=64)
   constexpr int VIN = 16 / sizeof(InT);   // elements per 16-byte load
   // The attention kernel launched behind this one may take SMs as this
   // grid's last CTAs retire (it waits for this grid's results).
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
-  const int sub = lane & (LPR - 1);  // position inside the row
+  const int sub = lane & (kProLanesPerRow - 1);  // position inside the row
   const int t = blockIdx.z;                      // 0 = Q, 1 = K, 2 = V
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
@@ -108,15 +100,15 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
   const float *gain = t == 0 ? p.q_gain : (t == 1 ? p.k_gain : nullptr);
   const bool rope = t < 2 && p.cos_t != nullptr;
   OutT *dst0 = out + ((long long)t * p.B * p.H + bh) * (long long)p.S * D + sub * E;
-  const int row_in_warp = lane / LPR;
-  const int s_base = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * RPW +
+  const int row_in_warp = lane / kProLanesPerRow;
+  const int s_base = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * kProRowsPerWarpStep +
                      row_in_warp;
   // All row groups' loads are issued before any is used, so a warp keeps
-  // STEPS * 16 * (E / VIN) bytes per lane in flight.
-  Pack<InT, VIN> raw[STEPS][E / VIN];
+  // kProSteps * 16 * (E / VIN) bytes per lane in flight.
+  Pack<InT, VIN> raw[kProSteps][E / VIN];
 #pragma unroll
-  for (int step = 0; step < STEPS; step++) {
-    const int s = s_base + step * RPW * kProWarps;
+  for (int step = 0; step < kProSteps; step++) {
+    const int s = s_base + step * kProRowsPerWarpStep * kProWarps;
     if (VEC && s < p.S) {
       const InT *src = src0 + (long long)s * rs;
 #pragma unroll
@@ -125,8 +117,8 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
     }
   }
 #pragma unroll
-  for (int step = 0; step < STEPS; step++) {
-    const int s = s_base + step * RPW * kProWarps;
+  for (int step = 0; step < kProSteps; step++) {
+    const int s = s_base + step * kProRowsPerWarpStep * kProWarps;
     // Lanes of a row group share the row, so the whole 8-lane group is in
     // or out together; shuffles stay inside the group.
     const bool in = s < p.S;
@@ -152,7 +144,7 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
 #pragma unroll
       for (int e = 0; e < E; e++) ss = __fmaf_rn(x[e], x[e], ss);
 #pragma unroll
-      for (int o = LPR / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      for (int o = kProLanesPerRow / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
       const float rms = rsqrtf(ss / (float)D + p.eps);
       const float *g = gain + ((p.split_row > 0 && grow >= p.split_row) ? D : 0) + sub * E;
 #pragma unroll
