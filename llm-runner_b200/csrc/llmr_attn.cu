@@ -324,7 +324,7 @@ int launch_prologue_t(llmr_ctx *ctx, const void *q, const void *k, const void *v
   View<InT> vq{static_cast<const InT *>(q), qs[0], qs[1], qs[2]};
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
-  const dim3 blocks((pp.S + kProRowsPerCta - 1) / kProRowsPerCta, pp.B * pp.H, 3);
+  const dim3 blocks = prologue_grid(pp.S, pp.B * pp.H);
   // 16-byte vector accesses per lane need 16-byte aligned bases and strides
   // that are whole 16-byte multiples (the tables' rows always are).
   constexpr int VIN = 16 / sizeof(InT);

@@ -132,7 +132,7 @@ int prologue(cudaStream_t st, int num_sms, const void *q, const void *k, const v
   View<InT> vk{static_cast<const InT *>(k), ks[0], ks[1], ks[2]};
   View<InT> vv{static_cast<const InT *>(v), vs[0], vs[1], vs[2]};
   (void)num_sms;
-  const dim3 blocks((pp.S + kProRowsPerCta - 1) / kProRowsPerCta, pp.B * pp.H, 3);
+  const dim3 blocks = prologue_grid(pp.S, pp.B * pp.H);
   auto ok = [&](const void *ptr, const long long *s) {
     return ptr == nullptr || ((reinterpret_cast<uintptr_t>(ptr) & 15) == 0 &&
                               (s == nullptr || (s[0] % VIN == 0 && s[1] % VIN == 0 && s[2] % VIN == 0)));

@@ -73,6 +73,19 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 // dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
 // applies on load, or fp32 for the exact path). VEC: every lane's slice of
 // the inputs and tables is 16-byte aligned (checked on the host).
+#ifndef LLMR_PRO_INTERLEAVE
+#define LLMR_PRO_INTERLEAVE 0
+#endif
+// Grid of prologue_kernel: (ceil(S / 128), B*H, 3), or with the tensor
+// interleaved into x, (3 * ceil(S / 128), B*H, 1).
+inline dim3 prologue_grid(int S, int BH) {
+  const int tb = (S + kProRowsPerCta - 1) / kProRowsPerCta;
+#if LLMR_PRO_INTERLEAVE
+  return dim3(3 * tb, BH, 1);
+#else
+  return dim3(tb, BH, 3);
+#endif
+}
 #ifndef LLMR_PRO_MIN_CTAS
 #define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
 #endif
@@ -87,7 +100,15 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int sub = lane & (kProLanesPerRow - 1);  // position inside the row
+#if LLMR_PRO_INTERLEAVE
+  // Tensor fastest: every wave of CTAs mixes the latency-bound Q/K rows
+  // (norm, RoPE) with the bandwidth-bound V casts.
+  const int t = blockIdx.x % 3;                  // 0 = Q, 1 = K, 2 = V
+  const int tblk = blockIdx.x / 3;               // 128-token block
+#else
   const int t = blockIdx.z;                      // 0 = Q, 1 = K, 2 = V
+  const int tblk = blockIdx.x;
+#endif
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
   // Select by value (a reference into the parameter block would force it
@@ -101,7 +122,7 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
   const bool rope = t < 2 && p.cos_t != nullptr;
   OutT *dst0 = out + ((long long)t * p.B * p.H + bh) * (long long)p.S * D + sub * E;
   const int row_in_warp = lane / kProLanesPerRow;
-  const int s_base = blockIdx.x * kProRowsPerCta + (threadIdx.x >> 5) * kProRowsPerWarpStep +
+  const int s_base = tblk * kProRowsPerCta + (threadIdx.x >> 5) * kProRowsPerWarpStep +
                      row_in_warp;
   // All row groups' loads are issued before any is used, so a warp keeps
   // kProSteps * 16 * (E / VIN) bytes per lane in flight.
