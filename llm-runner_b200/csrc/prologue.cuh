@@ -73,18 +73,9 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 // dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
 // applies on load, or fp32 for the exact path). VEC: every lane's slice of
 // the inputs and tables is 16-byte aligned (checked on the host).
-#ifndef LLMR_PRO_INTERLEAVE
-#define LLMR_PRO_INTERLEAVE 0
-#endif
-// Grid of prologue_kernel: (ceil(S / 128), B*H, 3), or with the tensor
-// interleaved into x, (3 * ceil(S / 128), B*H, 1).
+// Grid of prologue_kernel: (ceil(S / 128), B*H, 3).
 inline dim3 prologue_grid(int S, int BH) {
-  const int tb = (S + kProRowsPerCta - 1) / kProRowsPerCta;
-#if LLMR_PRO_INTERLEAVE
-  return dim3(3 * tb, BH, 1);
-#else
-  return dim3(tb, BH, 3);
-#endif
+  return dim3((S + kProRowsPerCta - 1) / kProRowsPerCta, BH, 3);
 }
 #ifndef LLMR_PRO_MIN_CTAS
 #define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
@@ -100,15 +91,8 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int sub = lane & (kProLanesPerRow - 1);  // position inside the row
-#if LLMR_PRO_INTERLEAVE
-  // Tensor fastest: every wave of CTAs mixes the latency-bound Q/K rows
-  // (norm, RoPE) with the bandwidth-bound V casts.
-  const int t = blockIdx.x % 3;                  // 0 = Q, 1 = K, 2 = V
-  const int tblk = blockIdx.x / 3;               // 128-token block
-#else
   const int t = blockIdx.z;                      // 0 = Q, 1 = K, 2 = V
-  const int tblk = blockIdx.x;
-#endif
+  const int tblk = blockIdx.x;                   // 128-token block
   const int bh = blockIdx.y;
   const int b = bh / p.H, h = bh - b * p.H;
   // Select by value (a reference into the parameter block would force it
