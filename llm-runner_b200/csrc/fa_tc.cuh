@@ -61,7 +61,8 @@ struct FaParams {
 // done, 2 + 2k / 3 + 2k producer begins unit k / its K'/V' are ready (k < 4),
 // 10 + 2k / 11 + 2k tile 0's first S of unit k ready / epilogue done,
 // 18 background Q' of unit 1 done, 19 background K'/V' pieces done,
-// 20 background done, 21 kernel end (all %globaltimer ns). Slots 32-63, SM
+// 20 background done, 21 kernel end, 22 past griddepcontrol.wait (all
+// %globaltimer ns). Slots 32-63, SM
 // clock cycles (clock64) of the softmax of tile 0, row 0, in blocks 4-11 of
 // the CTA's second unit: 32 + 4i S_j ready, +1 row max done, +2 P keys 0-63
 // handed over, +3 P keys 64-127 handed over (i = j - 4).
@@ -86,9 +87,9 @@ constexpr int kTimelineSlots = 64;
   } while (0)
 #endif
 
-// The prologue fused into the attention kernel (the fused op's default for
-// 16-bit inputs): the kernel itself writes the fp16 Q', K', V' its TMA maps
-// read. Work is cut into pieces of 32 token rows of one (tensor, b, h).
+// The prologue fused into the attention kernel (LLMR_FUSED_PROLOGUE, not the
+// default): the kernel itself writes the fp16 Q', K', V' its TMA maps read.
+// Work is cut into pieces of 32 token rows of one (tensor, b, h).
 //  * Start-up: every warp of every CTA writes the K'/V' pieces of the (b, h)
 //    pairs that the first round of units touches (spread round-robin over
 //    all warps of the grid), and the CTA's own warps write the Q' of its
@@ -385,6 +386,7 @@ __global__ void __launch_bounds__(384, 1)
   // Launched right behind the prologue (programmatic dependent launch), the
   // set-up above overlaps its tail; its output is read only after this.
   griddep_wait();
+  if (threadIdx.x == 0) LLMR_TL(22);
 
   const View<In> vq{static_cast<const In *>(fp.q), fp.qs[0], fp.qs[1], fp.qs[2]};
   const View<In> vk{static_cast<const In *>(fp.k), fp.ks[0], fp.ks[1], fp.ks[2]};

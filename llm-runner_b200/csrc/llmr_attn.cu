@@ -1098,7 +1098,8 @@ static int attention_core(llmr_ctx *ctx, const llmr_attn_desc *d, const void *q,
     const bool fused = !wide && nseq == 0 && d->in_dtype != LLMR_F32 && al(q) && al(k) &&
                        al(v) && st8(qs) && st8(ks) && st8(vs) && al(pp.q_gain) &&
                        al(pp.k_gain) && al(pp.cos_t) && al(pp.sin_t) &&
-                       (long long)B * H < (long long)kSyncInts && fused_prologue_enabled();
+                       !(d->flags & LLMR_MERGE) && (long long)B * H < (long long)kSyncInts &&
+                       fused_prologue_enabled();
     if (fused) {
       const long long rs = D, hs = (long long)S * D, bs = (long long)H * S * D;
       if ((rc = make_map(ctx, &mq, w, D, S, H, B, rs, hs, bs))) return rc;

@@ -2,8 +2,9 @@
 measured slower than the two-kernel default, kept as an option) gives exactly the output of the two-kernel path (prologue kernel,
 then the attention kernel), bit for bit: O in every output dtype and the
 LSE, for bf16 / fp16 inputs, D = 64 and 128, batch 2, ragged token counts,
-the txt/img gain split, a RoPE row offset, strided BHSD inputs and a long
-sequence where the start-up phase covers few heads. The two paths are
+the txt/img gain split, a RoPE row offset, strided BHSD inputs, a long
+sequence where the start-up phase covers few heads, and a grid where each
+CTA runs up to seven units (the background writer runs far ahead). The two paths are
 selected per process (LLMR_FUSED_PROLOGUE), so each runs in a child
 process on the same seeded inputs; the fused path is also checked to be one
 launch."""
@@ -68,6 +69,7 @@ CASES = [
     (128, 333, 30, 1, "bf16", "f32", "bhsd", 1),
     (128, 700, 2, 1, "bf16", "f32", "bshd", 0),     # RoPE without norm
     (128, 33792, 2, 1, "bf16", "f32", "bshd", 1),   # long: start-up covers one head
+    (64, 8192, 16, 2, "f16", "bf16", "bshd", 1),    # 1024 units: up to 7 per CTA
 ]
 
 
