@@ -88,8 +88,8 @@ int llmr_set_stream(llmr_ctx *ctx, void *stream);
 int llmr_ctx_set_sm_budget(llmr_ctx *ctx, int sms);
 /* Diagnostic builds only (compiled with -DLLMR_TIMELINE, `make TIMELINE=1`):
  * the D <= 128 attention kernel records per-CTA event timestamps
- * (64 slots per CTA, the slot meanings are listed in csrc/fa_tc.cuh) into
- * `device_buffer` (>= num_sms * 64 * 8 bytes; NULL
+ * (128 slots per CTA, the slot meanings are listed in csrc/fa_tc.cuh) into
+ * `device_buffer` (>= num_sms * 128 * 8 bytes; NULL
  * turns it off). Other builds return LLMR_EINVAL. No reference counterpart
  * (the reference's timer is per dispatch, dependencies/zimage.c3l/
  * dit.c3:17-26). */

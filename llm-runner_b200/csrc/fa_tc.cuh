@@ -62,11 +62,12 @@ struct FaParams {
 // 10 + 2k / 11 + 2k tile 0's first S of unit k ready / epilogue done,
 // 18 background Q' of unit 1 done, 19 background K'/V' pieces done,
 // 20 background done, 21 kernel end, 22 past griddepcontrol.wait (all
-// %globaltimer ns). Slots 32-63, SM
-// clock cycles (clock64) of the softmax of tile 0, row 0, in blocks 4-11 of
-// the CTA's second unit: 32 + 4i S_j ready, +1 row max done, +2 P keys 0-63
-// handed over, +3 P keys 64-127 handed over (i = j - 4).
-constexpr int kTimelineSlots = 64;
+// %globaltimer ns). Slots 32-127, SM clock cycles (clock64) in blocks 4-11
+// of the CTA's second unit (i = j - 4): the softmax of tile t, row 0, at
+// 32 + 32t + 4i S_j ready, +1 row max done, +2 P keys 0-63 handed over, +3 P
+// keys 64-127 handed over; the MMA warp at 96 + 4i + 2t + half, the issue of
+// the PV MMAs of that half of P_t (after their wait).
+constexpr int kTimelineSlots = 128;
 #ifdef LLMR_TIMELINE
 #define LLMR_TL(slot)                                                                    \
   do {                                                                                   \
@@ -526,10 +527,11 @@ __global__ void __launch_bounds__(384, 1)
                    (acc || ks > 0) ? 1u : 0u);
         }
       };
-      auto issue_o = [&](int t, int slot, bool acc, uint32_t parity) {
+      auto issue_o = [&](int t, int slot, bool acc, uint32_t parity, int tl) {
         for (int half = 0; half < 2; half++) {
           if (!mbar_wait(&p_half[2 * t + half], parity, abort_flag)) return false;
           tc_fence_after();
+          if (tl >= 0 && lane == 0) LLMR_TLC(tl + 2 * t + half);
           issue_o_half(t, slot, half, acc);
         }
         return true;
@@ -556,11 +558,12 @@ __global__ void __launch_bounds__(384, 1)
           const int uV = 2 * jj + 1, sV = uV % C::NST;
           const int uK = 2 * jj + 2, sK = uK % C::NST;
           const bool more = j + 1 < nblk;
+          const int tl = (k == 1 && j >= 4 && j < 12) ? 96 + 4 * (j - 4) : -1;
           if (!(ok = mbar_wait(&kv_full[sV], (uV / C::NST) & 1, abort_flag))) break;
           // O_t is overwritten by this unit's first PV: the previous unit's
           // epilogue must have read it.
           if (j == 0 && k > 0 && !(ok = mbar_wait(&o_empty[0], (k - 1) & 1, abort_flag))) break;
-          if (!(ok = issue_o(0, sV, j > 0, jj & 1))) break;
+          if (!(ok = issue_o(0, sV, j > 0, jj & 1, tl))) break;
           if (more) {
             if (!(ok = mbar_wait(&kv_full[sK], (uK / C::NST) & 1, abort_flag))) break;
             tc_fence_after();
@@ -570,7 +573,7 @@ __global__ void __launch_bounds__(384, 1)
             if (elect_one()) mma_commit(&o_full[0]);
           }
           if (j == 0 && k > 0 && !(ok = mbar_wait(&o_empty[1], (k - 1) & 1, abort_flag))) break;
-          if (!(ok = issue_o(1, sV, j > 0, jj & 1))) break;
+          if (!(ok = issue_o(1, sV, j > 0, jj & 1, tl))) break;
           if (elect_one()) mma_commit(&kv_empty[sV]);
           if (more) {
             issue_s(1, sK);
@@ -717,8 +720,9 @@ __global__ void __launch_bounds__(384, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], jj & 1, abort_flag));
         if (!ok) break;
         if (j == 0 && k < 4 && threadIdx.x == 0) LLMR_TL(10 + 2 * k);
-        const bool tl_blk = k == 1 && j >= 4 && j < 12 && threadIdx.x == 0;
-        if (tl_blk) LLMR_TLC(32 + 4 * (j - 4));
+        const bool tl_blk = k == 1 && j >= 4 && j < 12 && row == 0;
+        const int tl0 = 32 + 32 * t + 4 * (j - 4);
+        if (tl_blk) LLMR_TLC(tl0);
         tc_fence_after();
         const int valid = un.sk - j * C::BN;  // keys of this block inside the sequence
         // Applies the key mask (keys past the sequence -> -inf) to chunk c.
@@ -750,7 +754,7 @@ __global__ void __launch_bounds__(384, 1)
         // block's row max passes it by more than kMaxExp (P would overflow
         // fp16), and on the first block; O and l are rescaled then.
         const float m_new = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * sl2;
-        if (tl_blk) LLMR_TLC(33 + 4 * (j - 4));
+        if (tl_blk) LLMR_TLC(tl0 + 1);
         const bool need = m_new > m_used + kMaxExp;  // always true on block 0
         if (__any_sync(0xffffffffu, need)) {
           const float m_tgt = need ? m_new : m_used;
@@ -803,7 +807,7 @@ __global__ void __launch_bounds__(384, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_half[2 * t + (c == 3 ? 1 : 0)]);
-            if (tl_blk) LLMR_TLC(34 + (c == 3 ? 1 : 0) + 4 * (j - 4));
+            if (tl_blk) LLMR_TLC(tl0 + 2 + (c == 3 ? 1 : 0));
           }
         }
         const float2 s0 = f2_unpack(part2[0]), s1 = f2_unpack(part2[1]);

@@ -64,8 +64,11 @@ constexpr int kProWarps = 8;
 constexpr int kProSteps = 4;  // row groups per warp
 constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 128
 
-// Grid (ceil(S / 128), B*H, 3): blockIdx.z selects Q, K or V, blockIdx.y the
-// (b, h) unit. Q and K rows get the per-head RMSNorm of batch_head_norm
+// Grid (ceil(S / 128), 3, B*H): blockIdx.y selects Q, K or V, blockIdx.z the
+// (b, h) unit, last unit first. CTAs start roughly in grid order, so the
+// (b, h) units the attention kernel starts with (its first round of work
+// units is ordered by (b, h)) are written last and are still in L2 when it
+// loads them. Q and K rows get the per-head RMSNorm of batch_head_norm
 // (dependencies/zimage.c3l/shaders/zimage.slang:623-659:
 // x * (1/sqrt(mean(x^2) + eps)) * g) and the interleaved rotation of mrope
 // (dependencies/zimage.c3l/shaders/mrope.slang:47-53) in fp32, with the
@@ -73,9 +76,9 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 // dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
 // applies on load, or fp32 for the exact path). VEC: every lane's slice of
 // the inputs and tables is 16-byte aligned (checked on the host).
-// Grid of prologue_kernel: (ceil(S / 128), B*H, 3).
+// Grid of prologue_kernel: (ceil(S / 128), 3, B*H).
 inline dim3 prologue_grid(int S, int BH) {
-  return dim3((S + kProRowsPerCta - 1) / kProRowsPerCta, BH, 3);
+  return dim3((S + kProRowsPerCta - 1) / kProRowsPerCta, 3, BH);
 }
 #ifndef LLMR_PRO_MIN_CTAS
 #define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
@@ -91,9 +94,9 @@ __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int sub = lane & (kProLanesPerRow - 1);  // position inside the row
-  const int t = blockIdx.z;                      // 0 = Q, 1 = K, 2 = V
+  const int t = blockIdx.y;                      // 0 = Q, 1 = K, 2 = V
   const int tblk = blockIdx.x;                   // 128-token block
-  const int bh = blockIdx.y;
+  const int bh = gridDim.z - 1 - blockIdx.z;
   const int b = bh / p.H, h = bh - b * p.H;
   // Select by value (a reference into the parameter block would force it
   // into local memory).
