@@ -722,6 +722,7 @@ __global__ void __launch_bounds__(384, 1)
         if (j == 0 && k < 4 && threadIdx.x == 0) LLMR_TL(10 + 2 * k);
         const bool tl_blk = k == 1 && j >= 4 && j < 12 && row == 0;
         const int tl0 = 32 + 32 * t + 4 * (j - 4);
+        (void)tl0;  // read by the timeline stamps only
         if (tl_blk) LLMR_TLC(tl0);
         tc_fence_after();
         const int valid = un.sk - j * C::BN;  // keys of this block inside the sequence
