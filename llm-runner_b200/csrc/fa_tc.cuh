@@ -61,8 +61,9 @@ struct FaParams {
 // done, 2 + 2k / 3 + 2k producer begins unit k / its K'/V' are ready (k < 4),
 // 10 + 2k / 11 + 2k tile 0's first S of unit k ready / epilogue done,
 // 18 background Q' of unit 1 done, 19 background K'/V' pieces done,
-// 20 background done, 21 kernel end, 22 past griddepcontrol.wait (all
-// %globaltimer ns). Slots 32-127, SM clock cycles (clock64) in blocks 4-11
+// 20 background done, 21 kernel end, 22 past griddepcontrol.wait, for unit
+// k < 3 of tile 0: 23 + k its last P handed over, 26 + k its O complete
+// (epilogue starts), 29 + k its block 1's S ready (all %globaltimer ns). Slots 32-127, SM clock cycles (clock64) in blocks 4-11
 // of the CTA's second unit (i = j - 4): the softmax of tile t, row 0, at
 // 32 + 32t + 4i S_j ready, +1 row max done, +2 P keys 0-63 handed over, +3 P
 // keys 64-127 handed over; the MMA warp at 96 + 4i + 2t + half, the issue of
@@ -486,6 +487,22 @@ __global__ void __launch_bounds__(384, 1)
                             &kv_full[slot], c * 64, un.row0 + j * C::BN, h, b);
               issued = u + 1;
             }
+            // Halfway through a unit, the next unit's Q tiles and its first
+            // two K/V blocks are pulled into L2 (its first loads are HBM
+            // misses otherwise: Q is read by this CTA alone, and the K/V of
+            // a new (b, h) are not in L2 yet), so the unit boundary does not
+            // wait on HBM latency.
+            if (j == nblk / 2 && unit + (int)gridDim.x < p.units) {
+              const Unit nx = decode(unit + gridDim.x);
+              for (int t = 0; t < 2; t++)
+                for (int c = 0; c < C::NCHUNK; c++) {
+                  tma_prefetch_l2_4d(&tmQ, c * 64, nx.row0 + nx.q0 + t * C::BM, nx.h, nx.b);
+                  if (t * C::BN < nx.sk) {
+                    tma_prefetch_l2_4d(&tmK, c * 64, nx.row0 + t * C::BN, nx.h, nx.b);
+                    tma_prefetch_l2_4d(&tmV, c * 64, nx.row0 + t * C::BN, nx.h, nx.b);
+                  }
+                }
+            }
           }
           jb += nblk;
         }
@@ -720,6 +737,7 @@ __global__ void __launch_bounds__(384, 1)
         ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], jj & 1, abort_flag));
         if (!ok) break;
         if (j == 0 && k < 4 && threadIdx.x == 0) LLMR_TL(10 + 2 * k);
+        if (j == 1 && k < 3 && threadIdx.x == 0) LLMR_TL(29 + k);
         const bool tl_blk = k == 1 && j >= 4 && j < 12 && row == 0;
         const int tl0 = 32 + 32 * t + 4 * (j - 4);
         (void)tl0;  // read by the timeline stamps only
@@ -817,7 +835,9 @@ __global__ void __launch_bounds__(384, 1)
       jb += nblk;
       if (!ok) break;
       // ------------------------------------------------------- epilogue
+      if (k < 3 && threadIdx.x == 0) LLMR_TL(23 + k);
       ok = __all_sync(0xffffffffu, mbar_wait(&o_full[t], k & 1, abort_flag));
+      if (k < 3 && threadIdx.x == 0) LLMR_TL(26 + k);
       if (!ok) break;
       tc_fence_after();
       const int qloc = un.q0 + t * C::BM + row;  // query within its sequence

@@ -107,6 +107,14 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
 }
 
+// Prefetch of a 4-D tile of `map` into L2 (no shared memory, no barrier).
+__device__ __forceinline__ void tma_prefetch_l2_4d(const CUtensorMap *map, int c0, int c1,
+                                                   int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];"
+               ::"l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // 4-D tiled bulk tensor load into this CTA's shared memory, completing
 // `bytes` of transaction count on `bar`. c0 is the innermost coordinate.
 __device__ __forceinline__ void tma_load_4d(void *smem_dst,
