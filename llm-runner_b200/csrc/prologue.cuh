@@ -61,10 +61,13 @@ __device__ __forceinline__ void griddep_wait() {
 constexpr int kProLanesPerRow = 8;
 constexpr int kProRowsPerWarpStep = 32 / kProLanesPerRow;  // 4
 constexpr int kProWarps = 8;
-constexpr int kProSteps = 4;  // row groups per warp
-constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 128
+// Two row groups per warp keep a lane at 56 registers, so 4 CTAs (32 warps)
+// share an SM and hide the norm / table latency; 4 groups (80 registers,
+// 3 CTAs) ran 5 % slower, 1 group (47 registers, 5 CTAs) no faster.
+constexpr int kProSteps = 2;  // row groups per warp
+constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 64
 
-// Grid (ceil(S / 128), 3, B*H): blockIdx.y selects Q, K or V, blockIdx.z the
+// Grid (ceil(S / kProRowsPerCta), 3, B*H): blockIdx.y selects Q, K or V, blockIdx.z the
 // (b, h) unit, last unit first. CTAs start roughly in grid order, so the
 // (b, h) units the attention kernel starts with (its first round of work
 // units is ordered by (b, h)) are written last and are still in L2 when it
@@ -76,12 +79,12 @@ constexpr int kProRowsPerCta = kProRowsPerWarpStep * kProWarps * kProSteps;  // 
 // dense [3][B][H][S][D] in OutT (fp16 RNE, the rounding flash_attn.slang
 // applies on load, or fp32 for the exact path). VEC: every lane's slice of
 // the inputs and tables is 16-byte aligned (checked on the host).
-// Grid of prologue_kernel: (ceil(S / 128), 3, B*H).
+// Grid of prologue_kernel: (ceil(S / kProRowsPerCta), 3, B*H).
 inline dim3 prologue_grid(int S, int BH) {
   return dim3((S + kProRowsPerCta - 1) / kProRowsPerCta, 3, BH);
 }
 #ifndef LLMR_PRO_MIN_CTAS
-#define LLMR_PRO_MIN_CTAS 1  // CTAs per SM the register budget must allow
+#define LLMR_PRO_MIN_CTAS 4  // CTAs per SM the register budget must allow
 #endif
 template <int D, typename InT, typename OutT, bool VEC>
 __global__ void __launch_bounds__(256, LLMR_PRO_MIN_CTAS)
