@@ -720,7 +720,10 @@ def strong_scaling_block(args, world, rank, local):
     collective) and (b) the sequence-sharded ring with both K/V transports
     (copy-engine pulls; NCCL P2P with 0 / 8 / 16 SMs left free for NCCL's
     kernels). T1 is the same call on rank 0's GPU alone, timed here.
-    Every time is the max over ranks of CUDA-event time; each mode's
+    Every time is the max over ranks of CUDA-event time, taken in three
+    trials of `steps` calls each (all ranks together, a barrier before each
+    trial); the line carries the best trial (clock and power state drift by
+    several per cent between trials on these GPUs) and all three. Each mode's
     assembled output is checked on row windows against an fp64 restatement
     (max / mean error over all ranks)."""
     import numpy as np
@@ -746,28 +749,36 @@ def strong_scaling_block(args, world, rank, local):
     cfg = attn_config(case, S)
     steps = max(3, min(args.steps, 10))
     warm = 2
+    trials = 3
     stream = torch.cuda.Stream(device=dev)
+    trial_ms = {}
 
-    def timed(step_fn, ctx, active=True):
+    def timed(step_fn, ctx, active=True, key=None):
         with torch.cuda.stream(stream):
             if active:
                 for _ in range(warm):
                     step_fn()
             ctx.sync()
-            dist.barrier()
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(stream)
-            if active:
-                for _ in range(steps):
-                    step_fn()
-            b.record(stream)
-            torch.cuda.synchronize()
-            ctx.sync()
-        t = torch.tensor([a.elapsed_time(b) / steps if active else 0.0], dtype=torch.float64,
-                         device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        per_trial = []
+        for _ in range(trials):
+            with torch.cuda.stream(stream):
+                dist.barrier()
+                torch.cuda.synchronize()
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                if active:
+                    for _ in range(steps):
+                        step_fn()
+                b.record(stream)
+                torch.cuda.synchronize()
+                ctx.sync()
+            t = torch.tensor([a.elapsed_time(b) / steps if active else 0.0], dtype=torch.float64,
+                             device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            per_trial.append(float(t.item()))
+        if key is not None:
+            trial_ms[key] = per_trial
+        return min(per_trial)
 
     def check(err_max, err_sum, n):
         t = torch.tensor([err_max], dtype=torch.float64, device=dev)
@@ -778,6 +789,7 @@ def strong_scaling_block(args, world, rank, local):
 
     res = {"workload": f"{case.name}: B1 H{H} S{S} D{D} bf16, QK-RMSNorm + RoPE, one "
                        f"attention over {world} GPUs", "steps": steps, "warmup": warm,
+           "trials": trials, "timing": "best of the trials; each trial the max over ranks",
            "flop_per_call": case.flops}
     with torch.cuda.stream(stream):
         ctx = L.Context(local, stream=stream)
@@ -786,7 +798,7 @@ def strong_scaling_block(args, world, rank, local):
     ctx.reserve(3 * S * H * D * 2)
     t1 = timed(lambda: L.attention_fused(ctx, q, k, v, o_full, cfg, batch=1, seq_len=S,
                                          q_gain=qg, k_gain=kg, cos=cos, sin=sin),
-               ctx, active=rank == 0)
+               ctx, active=rank == 0, key="t1")
     res["t1_ms"] = t1
     windows = [(1008, 1072), (S - 32, S)]
 
@@ -794,7 +806,7 @@ def strong_scaling_block(args, world, rank, local):
     runs = partition_units(1, H, world, rank)
     hs_ms = timed(lambda: head_split_attention(ctx, q, k, v, o_full, cfg, batch=1, seq_len=S,
                                                rank=rank, world=world, q_gain=qg, k_gain=kg,
-                                               cos=cos, sin=sin), ctx)
+                                               cos=cos, sin=sin), ctx, key="headsplit")
     emax, esum, n = 0.0, 0.0, 0
     for _, h0, h1 in runs:
         for r0, r1 in windows:
@@ -818,11 +830,11 @@ def strong_scaling_block(args, world, rank, local):
                                    - reserve)
             ring = RingAttention(RingOps(rctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
                                  dev, transport=transport)
-        ms = timed(lambda: ring.forward(qs, ks, vs, o_loc, qg, kg, cos, sin), rctx)
+        key = "ring_copy" if transport == "copy" else f"ring_nccl_free_sms_{reserve}"
+        ms = timed(lambda: ring.forward(qs, ks, vs, o_loc, qg, kg, cos, sin), rctx, key=key)
         w0 = rank * s_loc
         want = f64_rows(q, k, v, qg, kg, cos, sin, case, range(w0, w0 + 64), range(H))
         err = (o_loc[0, :64].double() - want).abs()
-        key = "ring_copy" if transport == "copy" else f"ring_nccl_free_sms_{reserve}"
         res[key] = {"ms": ms, "efficiency": t1 / (world * ms),
                     **check(err.max().item(), err.sum().item(), err.numel())}
         torch.cuda.synchronize()
@@ -833,6 +845,7 @@ def strong_scaling_block(args, world, rank, local):
     tflops = {k_: case.flops / (v_["ms"] / 1e3) / 1e12 for k_, v_ in res.items()
               if isinstance(v_, dict) and "ms" in v_}
     res["tflops_whole_job"] = tflops
+    res["trial_ms"] = trial_ms
     return res
 
 
