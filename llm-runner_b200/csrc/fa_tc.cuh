@@ -63,11 +63,12 @@ struct FaParams {
 // 18 background Q' of unit 1 done, 19 background K'/V' pieces done,
 // 20 background done, 21 kernel end, 22 past griddepcontrol.wait, for unit
 // k < 3 of tile 0: 23 + k its last P handed over, 26 + k its O complete
-// (epilogue starts), 29 + k its block 1's S ready (all %globaltimer ns). Slots 32-127, SM clock cycles (clock64) in blocks 4-11
-// of the CTA's second unit (i = j - 4): the softmax of tile t, row 0, at
-// 32 + 32t + 4i S_j ready, +1 row max done, +2 P keys 0-63 handed over, +3 P
-// keys 64-127 handed over; the MMA warp at 96 + 4i + 2t + half, the issue of
-// the PV MMAs of that half of P_t (after their wait).
+// (epilogue starts), 29 + k its block 1's S ready (all %globaltimer ns).
+// Slots 32-127, SM clock cycles (clock64) in blocks 4-11 of the CTA's second
+// unit (i = j - 4): the softmax of tile t, row 0, at 32 + 32t + 4i S_j ready,
+// +1 row max done, +2 P keys 0-63 handed over, +3 P keys 64-127 handed over;
+// the MMA warp at 96 + 4i + 2t + half, the issue of the PV MMAs of that half
+// of P_t (after their wait).
 constexpr int kTimelineSlots = 128;
 #ifdef LLMR_TIMELINE
 #define LLMR_TL(slot)                                                                    \
