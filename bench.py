@@ -719,13 +719,16 @@ def strong_scaling_block(args, world, rank, local):
     ranks (strong scaling), as (a) a head split (H/N heads per GPU, no
     collective) and (b) the sequence-sharded ring with both K/V transports
     (copy-engine pulls; NCCL P2P with 0 / 8 / 16 SMs left free for NCCL's
-    kernels). T1 is the same call on rank 0's GPU alone, timed here.
-    Every time is the max over ranks of CUDA-event time, taken in three
-    trials of `steps` calls each (all ranks together, a barrier before each
-    trial); the line carries the best trial (clock and power state drift by
-    several per cent between trials on these GPUs) and all three. Each mode's
-    assembled output is checked on row windows against an fp64 restatement
-    (max / mean error over all ranks)."""
+    kernels). T1 is the whole call on one GPU: every rank runs it on its own
+    GPU at the same time (no communication) and rank 0's time is T1, so T1
+    and T_N are taken with every GPU busy, in the same power and clock state.
+    Each mode is timed in three trials (T1 and the head split alternate;
+    each ring mode follows with its own three): one trial = `steps` calls
+    after a barrier, its time the max over ranks of CUDA-event time; the line
+    carries each mode's best trial and all three (clocks drift by several per
+    cent over a run on these GPUs). Each mode's assembled output is checked
+    on row windows against an fp64 restatement (max / mean error over all
+    ranks)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -753,32 +756,30 @@ def strong_scaling_block(args, world, rank, local):
     stream = torch.cuda.Stream(device=dev)
     trial_ms = {}
 
-    def timed(step_fn, ctx, active=True, key=None):
+    def trial(step_fn, ctx, rank0_only=False):
+        """One trial: `steps` calls after a barrier; the max over ranks (rank
+        0's time when rank0_only), in ms per call."""
         with torch.cuda.stream(stream):
-            if active:
-                for _ in range(warm):
-                    step_fn()
+            dist.barrier()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(steps):
+                step_fn()
+            b.record(stream)
+            torch.cuda.synchronize()
             ctx.sync()
-        per_trial = []
-        for _ in range(trials):
-            with torch.cuda.stream(stream):
-                dist.barrier()
-                torch.cuda.synchronize()
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record(stream)
-                if active:
-                    for _ in range(steps):
-                        step_fn()
-                b.record(stream)
-                torch.cuda.synchronize()
-                ctx.sync()
-            t = torch.tensor([a.elapsed_time(b) / steps if active else 0.0], dtype=torch.float64,
-                             device=dev)
-            dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            per_trial.append(float(t.item()))
-        if key is not None:
-            trial_ms[key] = per_trial
-        return min(per_trial)
+        ms = a.elapsed_time(b) / steps
+        t = torch.tensor([ms if (rank == 0 or not rank0_only) else 0.0], dtype=torch.float64,
+                         device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def warm_up(step_fn, ctx):
+        with torch.cuda.stream(stream):
+            for _ in range(warm):
+                step_fn()
+            ctx.sync()
 
     def check(err_max, err_sum, n):
         t = torch.tensor([err_max], dtype=torch.float64, device=dev)
@@ -789,29 +790,36 @@ def strong_scaling_block(args, world, rank, local):
 
     res = {"workload": f"{case.name}: B1 H{H} S{S} D{D} bf16, QK-RMSNorm + RoPE, one "
                        f"attention over {world} GPUs", "steps": steps, "warmup": warm,
-           "trials": trials, "timing": "best of the trials; each trial the max over ranks",
+           "trials": trials,
+           "timing": "best of the trials; each trial the max over ranks (T1: rank 0, with "
+                     "every rank running the whole call on its own GPU at the same time)",
            "flop_per_call": case.flops}
     with torch.cuda.stream(stream):
         ctx = L.Context(local, stream=stream)
-    # T1: the whole call on one GPU (rank 0), the others idle.
-    o_full = torch.empty((1, S, H * D), dtype=torch.bfloat16, device=dev)
     ctx.reserve(3 * S * H * D * 2)
-    t1 = timed(lambda: L.attention_fused(ctx, q, k, v, o_full, cfg, batch=1, seq_len=S,
-                                         q_gain=qg, k_gain=kg, cos=cos, sin=sin),
-               ctx, active=rank == 0, key="t1")
+    o_t1 = torch.empty((1, S, H * D), dtype=torch.bfloat16, device=dev)
+    o_hs = torch.empty((1, S, H * D), dtype=torch.bfloat16, device=dev)
+    run_t1 = lambda: L.attention_fused(ctx, q, k, v, o_t1, cfg, batch=1, seq_len=S,
+                                       q_gain=qg, k_gain=kg, cos=cos, sin=sin)
+    run_hs = lambda: head_split_attention(ctx, q, k, v, o_hs, cfg, batch=1, seq_len=S,
+                                          rank=rank, world=world, q_gain=qg, k_gain=kg,
+                                          cos=cos, sin=sin)
+    # T1 and (a) the head split, alternating.
+    warm_up(run_t1, ctx)
+    warm_up(run_hs, ctx)
+    trial_ms["t1"], trial_ms["headsplit"] = [], []
+    for _ in range(trials):
+        trial_ms["t1"].append(trial(run_t1, ctx, rank0_only=True))
+        trial_ms["headsplit"].append(trial(run_hs, ctx))
+    t1 = min(trial_ms["t1"])
+    hs_ms = min(trial_ms["headsplit"])
     res["t1_ms"] = t1
     windows = [(1008, 1072), (S - 32, S)]
-
-    # (a) head split: H / world heads per GPU, no collective.
-    runs = partition_units(1, H, world, rank)
-    hs_ms = timed(lambda: head_split_attention(ctx, q, k, v, o_full, cfg, batch=1, seq_len=S,
-                                               rank=rank, world=world, q_gain=qg, k_gain=kg,
-                                               cos=cos, sin=sin), ctx, key="headsplit")
     emax, esum, n = 0.0, 0.0, 0
-    for _, h0, h1 in runs:
+    for _, h0, h1 in partition_units(1, H, world, rank):
         for r0, r1 in windows:
             want = f64_rows(q, k, v, qg, kg, cos, sin, case, range(r0, r1), range(h0, h1))
-            err = (o_full[0, r0:r1, h0 * D:h1 * D].double() - want).abs()
+            err = (o_hs[0, r0:r1, h0 * D:h1 * D].double() - want).abs()
             emax, esum, n = max(emax, err.max().item()), esum + err.sum().item(), n + err.numel()
     res["headsplit"] = {"ms": hs_ms, "efficiency": t1 / (world * hs_ms),
                         "heads_per_gpu": f"{H // world}" if H % world == 0 else "uneven",
@@ -831,7 +839,10 @@ def strong_scaling_block(args, world, rank, local):
             ring = RingAttention(RingOps(rctx, cfg, s_loc, rank * s_loc), H, D, S, rank, world,
                                  dev, transport=transport)
         key = "ring_copy" if transport == "copy" else f"ring_nccl_free_sms_{reserve}"
-        ms = timed(lambda: ring.forward(qs, ks, vs, o_loc, qg, kg, cos, sin), rctx, key=key)
+        run_ring = lambda: ring.forward(qs, ks, vs, o_loc, qg, kg, cos, sin)
+        warm_up(run_ring, rctx)
+        trial_ms[key] = [trial(run_ring, rctx) for _ in range(trials)]
+        ms = min(trial_ms[key])
         w0 = rank * s_loc
         want = f64_rows(q, k, v, qg, kg, cos, sin, case, range(w0, w0 + 64), range(H))
         err = (o_loc[0, :64].double() - want).abs()
